@@ -1,0 +1,366 @@
+// attention.cu -- GQA attention kernels.
+//  * attention_rows: one CTA per query row, exact softmax in the reference's
+//    order of operations (cpu_backend.rs:511-598, ops.rs:105-116): scores,
+//    optional additive mask, optional causal -inf triangle, max-subtracted
+//    exp, normalise, then sum_k p[k] * v[k] per output dim. Strided, so it
+//    serves both the trait op ([B, H, S, D] tensors) and the fused runtime
+//    (KV cache rows [ctx, Hkv, D]).
+//  * decode_attention: split-K flash decoding over the KV cache for one new
+//    token per sequence; each CTA owns one (sequence, KV head, key chunk) and
+//    all query heads of that KV head, so K/V are read once per group.
+#include <algorithm>
+
+#include "attention.h"
+#include "common.cuh"
+#include "internal.h"
+
+namespace bc {
+
+namespace {
+
+__device__ __forceinline__ float ldf(const void* p, int f16, int64_t i) {
+    return f16 ? __half2float(static_cast<const __half*>(p)[i]) : static_cast<const float*>(p)[i];
+}
+
+__global__ void attention_rows_kernel(const AttnRowsArgs a) {
+    extern __shared__ float sm[];
+    float* qs = sm;              // [D]
+    float* sc = sm + a.d;        // [skv]
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;  // over batch * heads * sq
+    const int64_t sq = row % a.sq, h = (row / a.sq) % a.heads, b = row / (a.sq * a.heads);
+    const int64_t kvh = h / (a.heads / a.kv_heads);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int64_t qoff = b * a.q_sb + h * a.q_sh + sq * a.q_ss;
+    for (int i = tid; i < a.d; i += blockDim.x) qs[i] = ldf(a.q, a.q_f16, qoff + i);
+    __syncthreads();
+    const int64_t kbase = b * a.kv_sb + kvh * a.kv_sh;
+    const int64_t limit = a.causal ? sq + (a.skv - a.sq) : a.skv - 1;  // last visible key
+    for (int64_t k = warp; k < a.skv; k += nw) {
+        float dot = 0.0f;
+        const int64_t ko = kbase + k * a.kv_ss;
+        for (int i = lane; i < a.d; i += 32) dot = fmaf(qs[i], ldf(a.k, a.kv_f16, ko + i), dot);
+        dot = warp_sum(dot);
+        if (lane == 0) {
+            float s = dot * a.scale;
+            if (a.mask) {
+                // cpu_backend.rs:560-575: a mask shorter than sq*skv applies only
+                // when its length equals skv
+                int64_t row_len = a.mask_numel >= a.sq * a.skv ? a.skv : a.mask_numel;
+                if (row_len == a.skv) {
+                    int64_t mo = sq * a.skv + k;
+                    if (mo < a.mask_numel) s += a.mask[mo];
+                }
+            }
+            if (k > limit) s += -INFINITY;
+            sc[k] = s;
+        }
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int64_t k = tid; k < a.skv; k += blockDim.x) m = fmaxf(m, sc[k]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (int i = 0; i < nw; ++i) m = fmaxf(m, red[i]);
+    __syncthreads();
+    float s = 0.0f;
+    for (int64_t k = tid; k < a.skv; k += blockDim.x) {
+        float e = expf(sc[k] - m);
+        sc[k] = e;
+        s += e;
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    s = 0.0f;
+    for (int i = 0; i < nw; ++i) s += red[i];
+    const float inv = 1.0f / s;
+    for (int64_t k = tid; k < a.skv; k += blockDim.x) sc[k] *= inv;
+    __syncthreads();
+    const int64_t ooff = b * a.o_sb + h * a.o_sh + sq * a.o_ss;
+    for (int i = tid; i < a.d; i += blockDim.x) {
+        float acc = 0.0f;
+        for (int64_t k = 0; k < a.skv; ++k) acc = fmaf(sc[k], ldf(a.v, a.kv_f16, kbase + k * a.kv_ss + i), acc);
+        a.out[ooff + i] = acc;
+    }
+}
+
+// Split-K decode attention -------------------------------------------------------
+// grid: (batch * kv_heads, nsplit). 4 warps; each warp takes 32-key blocks of
+// the CTA's chunk. Phase 1: lane = key, scores for the G query heads of this
+// KV head. Phase 2: lanes over head dims, acc += p * v. Online softmax per
+// warp, then merged across warps and written as one partial per split.
+template <int D, int G, typename KV>
+__global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a) {
+    constexpr int DPL = D / 32;  // head dims per lane in phase 2
+    __shared__ float qs[G][D];
+    __shared__ float ps[4][G][32];
+    __shared__ float wm[4][G], wl[4][G];
+    __shared__ float wacc[4][G][D];
+    const int bk = blockIdx.x, split = blockIdx.y;
+    const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // q rows of the G heads, pre-multiplied by the softmax scale
+    for (int i = tid; i < G * D; i += 128) {
+        int g = i / D, dd = i % D;
+        qs[g][dd] = a.q[((int64_t)b * a.heads + kvh * G + g) * D + dd] * a.scale;
+    }
+    __syncthreads();
+    const int kv_len = a.pos_ptr ? *a.pos_ptr + 1 : a.kv_len;
+    const int chunk = ((kv_len + a.nsplit - 1) / a.nsplit + 31) / 32 * 32;
+    const int64_t k0 = (int64_t)split * chunk;
+    const int64_t k1 = min((int64_t)kv_len, k0 + chunk);
+    const KV* kc = reinterpret_cast<const KV*>(a.k_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    const KV* vc = reinterpret_cast<const KV*>(a.v_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    const int64_t ks = (int64_t)a.kv_heads * D;  // key stride in elements
+    float m[G], l[G], acc[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[g][j] = 0.0f;
+    }
+    for (int64_t kb = k0 + warp * 32; kb < k1; kb += 128) {
+        const int64_t key = kb + lane;
+        const bool valid = key < k1;
+        float s[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[g] = 0.0f;
+        if (valid) {
+            const KV* kr = kc + key * ks;
+#pragma unroll 4
+            for (int dd = 0; dd < D; dd += 8) {
+                float kf[8];
+                if (sizeof(KV) == 2) {
+                    uint4 raw = *reinterpret_cast<const uint4*>(kr + dd);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float2 f = __half22float2(h2[j]);
+                        kf[2 * j] = f.x;
+                        kf[2 * j + 1] = f.y;
+                    }
+                } else {
+                    float4 x0 = *reinterpret_cast<const float4*>(kr + dd);
+                    float4 x1 = *reinterpret_cast<const float4*>(kr + dd + 4);
+                    kf[0] = x0.x; kf[1] = x0.y; kf[2] = x0.z; kf[3] = x0.w;
+                    kf[4] = x1.x; kf[5] = x1.y; kf[6] = x1.z; kf[7] = x1.w;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) s[g] = fmaf(qs[g][dd + j], kf[j], s[g]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float sv = valid ? s[g] : -INFINITY;
+            float bm = warp_max(sv);
+            float mn = fmaxf(m[g], bm);
+            float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
+            float p = valid ? expf(sv - mn) : 0.0f;
+            l[g] = l[g] * corr + warp_sum(p);
+            m[g] = mn;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[g][j] *= corr;
+            ps[warp][g][lane] = p;
+        }
+        __syncwarp();
+        const int nk = (int)min((int64_t)32, k1 - kb);
+        for (int j = 0; j < nk; ++j) {
+            const KV* vr = vc + (kb + j) * ks + lane * DPL;
+            float vf[DPL];
+            if (sizeof(KV) == 2) {
+#pragma unroll
+                for (int t = 0; t < DPL; t += 2) {
+                    float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr + t));
+                    vf[t] = f.x;
+                    vf[t + 1] = f.y;
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < DPL; ++t) vf[t] = reinterpret_cast<const float*>(vr)[t];
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float p = ps[warp][g][j];
+#pragma unroll
+                for (int t = 0; t < DPL; ++t) acc[g][t] = fmaf(p, vf[t], acc[g][t]);
+            }
+        }
+        __syncwarp();
+    }
+    // merge the 4 warps
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+#pragma unroll
+        for (int t = 0; t < DPL; ++t) wacc[warp][g][lane * DPL + t] = acc[g][t];
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += 128) {
+        const int g = i / D, dd = i % D;
+        float M = -INFINITY;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][g]);
+        float L = 0.0f, o = 0.0f;
+        for (int w = 0; w < 4; ++w) {
+            float c = wm[w][g] == -INFINITY ? 0.0f : expf(wm[w][g] - M);
+            L += wl[w][g] * c;
+            o += wacc[w][g][dd] * c;
+        }
+        const int64_t hb = ((int64_t)b * a.heads + kvh * G + g);
+        a.part_acc[(hb * a.nsplit + split) * D + dd] = o;
+        if (dd == 0) {
+            a.part_m[hb * a.nsplit + split] = M;
+            a.part_l[hb * a.nsplit + split] = L;
+        }
+    }
+}
+
+// One warp per (sequence, head): merge the splits and normalise.
+__global__ void decode_attn_combine_kernel(const DecodeAttnArgs a, int d) {
+    const int64_t hb = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (hb >= (int64_t)a.batch * a.heads) return;
+    float M = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, a.part_m[hb * a.nsplit + s]);
+    float L = 0.0f;
+    for (int s = 0; s < a.nsplit; ++s) {
+        float mm = a.part_m[hb * a.nsplit + s];
+        L += mm == -INFINITY ? 0.0f : a.part_l[hb * a.nsplit + s] * expf(mm - M);
+    }
+    const float inv = 1.0f / L;
+    for (int dd = lane; dd < d; dd += 32) {
+        float o = 0.0f;
+        for (int s = 0; s < a.nsplit; ++s) {
+            float mm = a.part_m[hb * a.nsplit + s];
+            if (mm != -INFINITY) o += a.part_acc[(hb * a.nsplit + s) * d + dd] * expf(mm - M);
+        }
+        a.out[hb * d + dd] = o * inv;
+    }
+}
+
+template <int D, int G>
+void launch_decode_t(const DecodeAttnArgs& a, cudaStream_t s) {
+    dim3 grid((unsigned)(a.batch * a.kv_heads), (unsigned)a.nsplit);
+    if (a.kv_f16)
+        decode_attn_kernel<D, G, __half><<<grid, 128, 0, s>>>(a);
+    else
+        decode_attn_kernel<D, G, float><<<grid, 128, 0, s>>>(a);
+    BC_LAUNCHED("decode_attn_kernel");
+}
+
+}  // namespace
+
+void launch_attention_rows(const AttnRowsArgs& a, cudaStream_t s) {
+    const int64_t rows = a.batch * a.heads * a.sq;
+    if (rows == 0 || a.skv == 0) return;
+    const size_t smem = (size_t)(a.d + a.skv) * sizeof(float);
+    if (smem > 200 * 1024) shape_err("attention: key length too long for the single-row kernel");
+    if (smem > 48 * 1024)
+        BC_CUDA(cudaFuncSetAttribute(attention_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attention_rows_kernel<<<(unsigned)rows, 128, smem, s>>>(a);
+    BC_LAUNCHED("attention_rows_kernel");
+}
+
+int plan_decode_splits(int batch, int kv_heads, int kv_len, int sm_count, int max_splits) {
+    const int64_t want = 2LL * sm_count;
+    int64_t per = std::max<int64_t>(1, (int64_t)batch * kv_heads);
+    int64_t ns = (want + per - 1) / per;
+    ns = std::min<int64_t>(ns, (kv_len + 127) / 128);  // at least 128 keys (one per lane-warp pass) each
+    ns = std::max<int64_t>(1, std::min<int64_t>(ns, max_splits));
+    return (int)ns;
+}
+
+bool decode_attention_supported(int head_dim, int group) {
+    return (head_dim == 64 || head_dim == 128) && (group == 1 || group == 2 || group == 4 || group == 8);
+}
+
+void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s) {
+    const int G = a.heads / a.kv_heads;
+    if (!decode_attention_supported(a.d, G)) fail(BEACON_CUDA_ERR_SHAPE_MISMATCH, "decode attention: unsupported head shape");
+if (a.d == 128) {
+        if (G == 8) launch_decode_t<128, 8>(a, s);
+        else if (G == 4) launch_decode_t<128, 4>(a, s);
+        else if (G == 2) launch_decode_t<128, 2>(a, s);
+        else launch_decode_t<128, 1>(a, s);
+    } else {
+        if (G == 8) launch_decode_t<64, 8>(a, s);
+        else if (G == 4) launch_decode_t<64, 4>(a, s);
+        else if (G == 2) launch_decode_t<64, 2>(a, s);
+        else launch_decode_t<64, 1>(a, s);
+    }
+    const int64_t warps = (int64_t)a.batch * a.heads;
+    decode_attn_combine_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(a, a.d);
+    BC_LAUNCHED("decode_attn_combine_kernel");
+}
+
+}  // namespace bc
+
+using namespace bc;
+
+extern "C" int32_t beacon_cuda_op_attention(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                            const BeaconCudaTensor* q, const BeaconCudaTensor* k,
+                                            const BeaconCudaTensor* v, const BeaconCudaTensor* mask, float scale,
+                                            int32_t causal, BeaconCudaTensor** out) {
+    return guard([&]() -> int32_t {
+        require(ctx && stream && q && k && v && out, "attention: null argument");
+        set_device(ctx);
+        if (q->shape.size() != 4 || k->shape.size() != 4 || v->shape.size() != 4)
+            shape_err("attention: q/k/v must be 4-D");  // cpu_backend.rs:518-522
+        auto isf = [](const BeaconCudaTensor* t) {
+            return t->dtype == BEACON_CUDA_DTYPE_F32 || t->dtype == BEACON_CUDA_DTYPE_F16;
+        };
+        if (!isf(q) || !isf(k) || !isf(v) || k->dtype != v->dtype)
+            fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "attention: q/k/v must be F32 or F16 (k and v alike)");
+        const int64_t B = q->shape[0], H = q->shape[1], Sq = q->shape[2], D = q->shape[3];
+        const int64_t Hkv = k->shape[1], Skv = k->shape[2];
+        if (k->shape != v->shape || k->shape[0] != B || k->shape[3] != D) shape_err("attention: k/v shape mismatch");
+        if (Hkv == 0 || H % Hkv) shape_err("attention: n_heads must be divisible by n_kv_heads");
+        if (mask && mask->dtype != BEACON_CUDA_DTYPE_F32) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "attention: mask must be F32");
+        if (causal < -1 || causal > 1) invalid("attention: causal must be -1, 0 or 1");
+        const bool use_causal = causal == 1 || (causal == -1 && !mask && Sq > 1);
+        if (use_causal && Skv < Sq) shape_err("attention: causal needs at least as many keys as queries");
+        BeaconCudaTensor* o = new_tensor(ctx, q->shape, BEACON_CUDA_DTYPE_F32);
+        try {
+            AttnRowsArgs a{};
+            a.q = q->data();
+            a.q_f16 = q->dtype == BEACON_CUDA_DTYPE_F16;
+            a.k = k->data();
+            a.v = v->data();
+            a.kv_f16 = k->dtype == BEACON_CUDA_DTYPE_F16;
+            a.out = static_cast<float*>(o->data());
+            a.mask = mask ? static_cast<const float*>(mask->data()) : nullptr;
+            a.mask_numel = mask ? mask->numel() : 0;
+            a.batch = B;
+            a.heads = H;
+            a.kv_heads = Hkv;
+            a.sq = Sq;
+            a.skv = Skv;
+            a.d = (int)D;
+            a.scale = scale;
+            a.causal = use_causal ? 1 : 0;
+            a.q_sb = H * Sq * D;
+            a.q_sh = Sq * D;
+            a.q_ss = D;
+            a.kv_sb = Hkv * Skv * D;
+            a.kv_sh = Skv * D;
+            a.kv_ss = D;
+            a.o_sb = H * Sq * D;
+            a.o_sh = Sq * D;
+            a.o_ss = D;
+            launch_attention_rows(a, stream->s);
+        } catch (...) {
+            delete o;
+            throw;
+        }
+        *out = o;
+        return BEACON_CUDA_OK;
+    });
+}

@@ -1,0 +1,54 @@
+// attention.h -- argument blocks of the attention kernels (attention.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace bc {
+
+// Strided exact attention, one CTA per query row. Element offsets:
+// q/out: b*sb + h*sh + s*ss; k/v: b*kv_sb + kvh*kv_sh + key*kv_ss.
+struct AttnRowsArgs {
+    const void* q;
+    int q_f16;
+    const void* k;
+    const void* v;
+    int kv_f16;
+    float* out;
+    const float* mask;
+    int64_t mask_numel;
+    int64_t batch, heads, kv_heads, sq, skv;
+    int d;
+    float scale;
+    int causal;
+    int64_t q_sb, q_sh, q_ss;
+    int64_t kv_sb, kv_sh, kv_ss;
+    int64_t o_sb, o_sh, o_ss;
+};
+void launch_attention_rows(const AttnRowsArgs& a, cudaStream_t s);
+
+// Split-K decode attention over KV caches laid out [batch][max_ctx][kv_heads][d].
+// q: f32 [batch][heads][d]; out: f32 [batch][heads][d]. Scratch: part_acc
+// [batch*heads*nsplit*d], part_m / part_l [batch*heads*nsplit].
+struct DecodeAttnArgs {
+    const float* q;
+    const void* k_cache;
+    const void* v_cache;
+    int kv_f16;
+    int64_t cache_sb;  // elements between sequences
+    int batch, heads, kv_heads, d;
+    int kv_len;        // keys [0, kv_len) are attended ...
+    const int* pos_ptr;  // ... or, when set, keys [0, *pos_ptr + 1) (graph replay)
+    float scale;
+    int nsplit;
+    float* part_acc;
+    float* part_m;
+    float* part_l;
+    float* out;
+};
+int plan_decode_splits(int batch, int kv_heads, int kv_len, int sm_count, int max_splits);
+bool decode_attention_supported(int head_dim, int group);
+void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s);
+
+}  // namespace bc

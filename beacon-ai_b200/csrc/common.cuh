@@ -1,0 +1,122 @@
+// common.cuh -- device helpers shared by the kernels of libbeacon_cuda.so.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace bc {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float bits_f32(uint32_t b) { return __uint_as_float(b); }
+__device__ __forceinline__ uint32_t f32_bits(float f) { return __float_as_uint(f); }
+
+// Half -> single exactly as dequant.rs:80-109 does it (payload-preserving for
+// NaN, exact for subnormals). Written with integer operations so that NaN
+// payloads survive, which the hardware conversion does not promise.
+__host__ __device__ __forceinline__ uint32_t f16_to_f32_bits(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t exponent = (h >> 10) & 0x1Fu;
+    uint32_t mantissa = h & 0x3FFu;
+    if (exponent == 0) {
+        if (mantissa == 0) return sign;
+        // normalise: shift the leading one into bit 10
+#ifdef __CUDA_ARCH__
+        int lz = __clz((int)mantissa) - 21;  // zeros above bit 10 in an 11-bit field
+#else
+        int lz = __builtin_clz(mantissa) - 21;
+#endif
+        uint32_t m = (mantissa << lz) & 0x3FFu;
+        int32_t e = -14 - lz;
+        return sign | ((uint32_t)(e + 127) << 23) | (m << 13);
+    }
+    if (exponent == 31) return sign | 0x7F800000u | (mantissa << 13);
+    return sign | ((exponent + 112) << 23) | (mantissa << 13);
+}
+
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+    // For finite inputs (every scale in practice) the hardware conversion is
+    // exact; keep the integer path so NaN payloads match the reference.
+    return bits_f32(f16_to_f32_bits(h));
+}
+
+// Single -> half with truncation, dequant.rs:116-152 restated on integers:
+// flush below 2^-24 to zero, overflow to Inf, NaN keeps (payload >> 13) >= 1.
+__device__ __forceinline__ uint16_t f32_to_f16_rtz(float v) {
+    uint32_t bits = f32_bits(v);
+    uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+    int32_t exponent = (int32_t)((bits >> 23) & 0xFFu);
+    uint32_t mantissa = bits & 0x007FFFFFu;
+    if (exponent == 255) {
+        if (mantissa == 0) return sign | 0x7C00u;
+        uint32_t m = mantissa >> 13;
+        return sign | 0x7C00u | (uint16_t)(m < 1u ? 1u : m);
+    }
+    int32_t new_exp = exponent - 112;
+    if (new_exp >= 31) return sign | 0x7C00u;
+    if (new_exp <= 0) {
+        if (new_exp < -10) return sign;
+        return sign | (uint16_t)((mantissa | 0x00800000u) >> (14 - new_exp));
+    }
+    return sign | (uint16_t)((uint32_t)new_exp << 10) | (uint16_t)(mantissa >> 13);
+}
+
+// The reference's arithmetic runs on x86 SSE (or AArch64 with the same
+// propagation for one NaN operand): a NaN operand comes out quieted, an
+// invalid operation (0*Inf, Inf-Inf) yields the default NaN 0xFFC00000. GPU
+// arithmetic returns a canonical NaN instead, so the bit-exact dequant kernel
+// fixes the result up after each operation.
+__device__ __forceinline__ float x86_nan(float r, float a, float b) {
+    if (!isnan(r)) return r;
+    if (isnan(a)) return bits_f32(f32_bits(a) | 0x00400000u);
+    if (isnan(b)) return bits_f32(f32_bits(b) | 0x00400000u);
+    return bits_f32(0xFFC00000u);
+}
+__device__ __forceinline__ float x86_mul(float a, float b) { return x86_nan(__fmul_rn(a, b), a, b); }
+__device__ __forceinline__ float x86_sub(float a, float b) { return x86_nan(__fsub_rn(a, b), a, b); }
+
+// dp2a: d = c + a.h0 * b.byte(0|2) + a.h1 * b.byte(1|3); `a` holds two signed
+// 16-bit values, `b` four 8-bit values (unsigned or signed).
+__device__ __forceinline__ int dp2a_lo_u8(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_u8(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_lo_s8(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_s8(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// 128-bit read-only load that does not allocate in L1 (weights are streamed once).
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+}  // namespace bc

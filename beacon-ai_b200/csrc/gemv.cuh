@@ -1,0 +1,556 @@
+// gemv.cuh -- fused GGUF dequant + GEMV (decode, batch 1-16) for sm_100a.
+//
+// Replaces the reference's quantized GEMV (q4_matmul_f32, ops.rs:62-70, and
+// the row loop of q4_dot_f32, ops.rs:38-56) and serves
+// ComputeBackend::quantized_matmul (backend.rs:32-41) for small batches.
+//
+// Design (HBM-bound, ~0.56 B of weight per multiply-add):
+//  * weights in row-group tiles (QLayout): 32 rows x 256 columns; lane l of a
+//    warp owns row l, so every warp-wide 128-bit load reads 512 contiguous
+//    bytes and no cross-lane reduction is needed;
+//  * the activation slice of the CTA is staged once in shared memory and read
+//    as broadcasts (every lane of a warp reads the same address);
+//  * FAST mode: activations quantized per 32 elements to int16, products
+//    summed exactly with dp2a against the unsigned 4-bit / signed 8-bit codes,
+//    block scales applied once per block in f32;
+//    F32 mode: f32 activations times the reference's f32 weight value
+//    (optionally truncated to f16 as the CPU engine's weights are);
+//  * 4 warps split the CTA's tiles; optional split-K over CTAs with a
+//    deterministic last-arriver reduction (fixed summation order).
+#pragma once
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace bc {
+
+enum { FMT_Q4_0 = 0, FMT_Q8_0 = 1, FMT_Q4_K = 2 };
+
+template <int FMT>
+struct Fmt {
+    static constexpr int CH = (FMT == FMT_Q8_0) ? 16 : 8;  // 16-byte chunks per row per tile
+};
+
+struct GemvParams {
+    const uint8_t* w;
+    int64_t ktiles;
+    int64_t tile_bytes;
+    int64_t n;      // rows of W that hold data
+    int64_t n_pad;  // rows of the tiled layout
+    int tps;
+    int ksplit;
+    const void* x;
+    int x_f16;
+    int64_t x_ld;
+    int64_t k;  // logical columns; staged elements beyond k are zero
+    int batch;
+    float* y;
+    int64_t y_ld;
+    const float* res;
+    int64_t res_ld;
+    float* partial;
+    int* counters;
+    int rtz;
+};
+
+__device__ __forceinline__ float load_x(const GemvParams& p, int b, int64_t kk) {
+    if (b >= p.batch || kk >= p.k) return 0.0f;
+    if (p.x_f16) return __half2float(reinterpret_cast<const __half*>(p.x)[b * p.x_ld + kk]);
+    return reinterpret_cast<const float*>(p.x)[b * p.x_ld + kk];
+}
+
+// Small integer q (0 <= q < 2^22) to float with one OR and one FADD:
+// 2^23 + q is exact in f32, subtract 2^23 + bias.
+__device__ __forceinline__ float small_int_f32(uint32_t q, float magic_plus_bias) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | q), magic_plus_bias);
+}
+
+__device__ __forceinline__ float f16_round_trip_rtz(float v) {
+    return __uint_as_float(f16_to_f32_bits(f32_to_f16_rtz(v)));
+}
+
+// Shared-memory staging -------------------------------------------------------
+// F32 mode:  float xs[B][span]
+// FAST mode: int16 xq[B][span] (Q4_0: each 8-element group stored as
+//            e0 e2 e4 e6 e1 e3 e5 e7 to match the interleaved nibbles),
+//            float sx[B][span/32], int sq[B][span/32] (sum of the int16s).
+template <int FMT, int MODE, int B>
+__device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* smem, int64_t k_base,
+                                        int span) {
+    if (MODE == MODE_F32) {
+        float* xs = reinterpret_cast<float*>(smem);
+        for (int i = threadIdx.x; i < B * span; i += blockDim.x) {
+            int b = i / span, e = i - b * span;
+            xs[i] = load_x(p, b, k_base + e);
+        }
+    } else {
+        int16_t* xq = reinterpret_cast<int16_t*>(smem);
+        const int nblk = span / 32;
+        float* sx = reinterpret_cast<float*>(smem + (size_t)B * span * 2);
+        int* sq = reinterpret_cast<int*>(sx + B * nblk);
+        for (int i = threadIdx.x; i < B * nblk; i += blockDim.x) {
+            int b = i / nblk, j = i - b * nblk;
+            float v[32];
+            float amax = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                v[e] = load_x(p, b, k_base + j * 32 + e);
+                amax = fmaxf(amax, fabsf(v[e]));
+            }
+            float inv = amax > 0.0f ? __fdiv_rn(32767.0f, amax) : 0.0f;
+            int qv[32];
+            int sum = 0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                int q = __float2int_rn(__fmul_rn(v[e], inv));
+                q = max(-32767, min(32767, q));
+                qv[e] = q;
+                sum += q;
+            }
+            uint32_t packed[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+                int a0, a1;
+                if (FMT == FMT_Q4_0) {
+                    // slot s of an 8-group holds element (s<4 ? 2s : 2(s-4)+1)
+                    int grp = e & ~7, s0 = e & 7, s1 = s0 + 1;
+                    int e0 = grp + (s0 < 4 ? 2 * s0 : 2 * (s0 - 4) + 1);
+                    int e1 = grp + (s1 < 4 ? 2 * s1 : 2 * (s1 - 4) + 1);
+                    a0 = qv[e0];
+                    a1 = qv[e1];
+                } else {
+                    a0 = qv[e];
+                    a1 = qv[e + 1];
+                }
+                packed[e / 2] = (uint32_t)(a0 & 0xFFFF) | ((uint32_t)a1 << 16);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(xq + (size_t)b * span + j * 32);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                    packed[4 * c + 3]);
+            sx[b * nblk + j] = amax > 0.0f ? __fdiv_rn(amax, 32767.0f) : 0.0f;
+            sq[b * nblk + j] = sum;
+        }
+    }
+}
+
+// Tile consumers --------------------------------------------------------------
+
+__device__ __forceinline__ float half_at(const uint4& m, int i) {
+    uint32_t w = (&m.x)[i >> 1];
+    uint16_t h = (uint16_t)((i & 1) ? (w >> 16) : (w & 0xFFFF));
+    return f16_to_f32(h);
+}
+
+template <int B>
+__device__ __forceinline__ void fma8(float (&acc)[B], const float (&w)[8], const float* xs, int span,
+                                     int e0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        const float4* xp = reinterpret_cast<const float4*>(xs + (size_t)b * span + e0);
+        float4 xa = xp[0], xb = xp[1];
+        acc[b] = fmaf(w[0], xa.x, acc[b]);
+        acc[b] = fmaf(w[1], xa.y, acc[b]);
+        acc[b] = fmaf(w[2], xa.z, acc[b]);
+        acc[b] = fmaf(w[3], xa.w, acc[b]);
+        acc[b] = fmaf(w[4], xb.x, acc[b]);
+        acc[b] = fmaf(w[5], xb.y, acc[b]);
+        acc[b] = fmaf(w[6], xb.z, acc[b]);
+        acc[b] = fmaf(w[7], xb.w, acc[b]);
+    }
+}
+
+template <int B>
+__device__ __forceinline__ void fma4(float (&acc)[B], const float (&w)[4], const float* xs, int span,
+                                     int e0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        float4 xa = *reinterpret_cast<const float4*>(xs + (size_t)b * span + e0);
+        acc[b] = fmaf(w[0], xa.x, acc[b]);
+        acc[b] = fmaf(w[1], xa.y, acc[b]);
+        acc[b] = fmaf(w[2], xa.z, acc[b]);
+        acc[b] = fmaf(w[3], xa.w, acc[b]);
+    }
+}
+
+// Q4_0: meta = 8 f16 block scales; chunk c = block c, byte i -> elements 2i, 2i+1.
+template <int MODE, int B>
+__device__ __forceinline__ void consume_q4_0(const uint4& meta, const uint4 (&q)[8], const uint8_t* smem,
+                                             int span, int tile, float (&acc)[B], bool rtz) {
+    if (MODE == MODE_F32) {
+        const float* xs = reinterpret_cast<const float*>(smem);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float d = half_at(meta, c);
+            const uint32_t* wq = &q[c].x;
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+                float w[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t byte = (wq[wd] >> (8 * j)) & 0xFFu;
+                    float lo = small_int_f32(byte & 0xFu, 8388616.0f);  // q - 8
+                    float hi = small_int_f32(byte >> 4, 8388616.0f);
+                    w[2 * j] = __fmul_rn(lo, d);
+                    w[2 * j + 1] = __fmul_rn(hi, d);
+                    if (rtz) {
+                        w[2 * j] = f16_round_trip_rtz(w[2 * j]);
+                        w[2 * j + 1] = f16_round_trip_rtz(w[2 * j + 1]);
+                    }
+                }
+                fma8<B>(acc, w, xs, span, tile * 256 + c * 32 + wd * 8);
+            }
+        }
+    } else {
+        const int16_t* xq = reinterpret_cast<const int16_t*>(smem);
+        const int nblk = span / 32;
+        const float* sx = reinterpret_cast<const float*>(smem + (size_t)B * span * 2);
+        const int* sq = reinterpret_cast<const int*>(sx + B * nblk);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float d = half_at(meta, c);
+            const uint32_t* wq = &q[c].x;
+            uint32_t lo[4], hi[4];
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+                lo[wd] = wq[wd] & 0x0F0F0F0Fu;
+                hi[wd] = (wq[wd] >> 4) & 0x0F0F0F0Fu;
+            }
+            const int blk = tile * 8 + c;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)b * span + blk * 32);
+                int ai = 0;
+#pragma unroll
+                for (int wd = 0; wd < 4; ++wd) {
+                    int4 X = xp[wd];
+                    ai = dp2a_lo_u8(X.x, lo[wd], ai);
+                    ai = dp2a_hi_u8(X.y, lo[wd], ai);
+                    ai = dp2a_lo_u8(X.z, hi[wd], ai);
+                    ai = dp2a_hi_u8(X.w, hi[wd], ai);
+                }
+                const int bi = b * nblk + blk;
+                acc[b] = fmaf(d * sx[bi], (float)(ai - 8 * sq[bi]), acc[b]);
+            }
+        }
+    }
+}
+
+// Q8_0: meta = 8 f16 block scales; chunks 2c, 2c+1 = the 32 int8 codes of block c.
+template <int MODE, int B>
+__device__ __forceinline__ void consume_q8_0(const uint4& meta, const uint4 (&q)[16], const uint8_t* smem,
+                                             int span, int tile, float (&acc)[B], bool rtz) {
+    if (MODE == MODE_F32) {
+        const float* xs = reinterpret_cast<const float*>(smem);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            const float d = half_at(meta, c >> 1);
+            const uint32_t* wq = &q[c].x;
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+                float w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t u = ((wq[wd] >> (8 * j)) & 0xFFu) ^ 0x80u;  // int8 + 128
+                    w[j] = __fmul_rn(small_int_f32(u, 8388736.0f), d);
+                    if (rtz) w[j] = f16_round_trip_rtz(w[j]);
+                }
+                fma4<B>(acc, w, xs, span, tile * 256 + c * 16 + wd * 4);
+            }
+        }
+    } else {
+        const int16_t* xq = reinterpret_cast<const int16_t*>(smem);
+        const int nblk = span / 32;
+        const float* sx = reinterpret_cast<const float*>(smem + (size_t)B * span * 2);
+#pragma unroll
+        for (int bl = 0; bl < 8; ++bl) {
+            const float d = half_at(meta, bl);
+            const int blk = tile * 8 + bl;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)b * span + blk * 32);
+                int ai = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t* wq = &q[2 * bl + h].x;
+                    int4 X = xp[2 * h], Y = xp[2 * h + 1];
+                    ai = dp2a_lo_s8(X.x, wq[0], ai);
+                    ai = dp2a_hi_s8(X.y, wq[0], ai);
+                    ai = dp2a_lo_s8(X.z, wq[1], ai);
+                    ai = dp2a_hi_s8(X.w, wq[1], ai);
+                    ai = dp2a_lo_s8(Y.x, wq[2], ai);
+                    ai = dp2a_hi_s8(Y.y, wq[2], ai);
+                    ai = dp2a_lo_s8(Y.z, wq[3], ai);
+                    ai = dp2a_hi_s8(Y.w, wq[3], ai);
+                }
+                acc[b] = fmaf(d * sx[b * nblk + blk], (float)ai, acc[b]);
+            }
+        }
+    }
+}
+
+// decode_k_scales_mins (dequant.rs:289-307) from the 12 packed bytes in
+// meta words 1..3.
+__device__ __forceinline__ void k_scales(const uint4& meta, int (&sc)[8], int (&mn)[8]) {
+    uint8_t q[12];
+#pragma unroll
+    for (int i = 0; i < 12; ++i) q[i] = (uint8_t)((&meta.y)[i >> 2] >> (8 * (i & 3)));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = q[j] & 0x3F;
+        mn[j] = q[j + 4] & 0x3F;
+    }
+#pragma unroll
+    for (int j = 4; j < 8; ++j) {
+        sc[j] = (q[j + 4] & 0x0F) | ((q[j - 4] >> 6) << 4);
+        mn[j] = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Q4_K: meta = [d, dmin, 12 scale bytes]; chunk c: pair p = c/2, half h = c%2,
+// byte i -> element 64p+16h+i (low nibble, sub-block 2p) and
+// 64p+32+16h+i (high nibble, sub-block 2p+1).
+template <int MODE, int B>
+__device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)[8], const uint8_t* smem,
+                                             int span, int tile, float (&acc)[B], bool rtz) {
+    const float d = f16_to_f32((uint16_t)(meta.x & 0xFFFF));
+    const float dmin = f16_to_f32((uint16_t)(meta.x >> 16));
+    int sc[8], mn[8];
+    k_scales(meta, sc, mn);
+    if (MODE == MODE_F32) {
+        const float* xs = reinterpret_cast<const float*>(smem);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const int pr = c >> 1, h = c & 1;
+            const float sl = __fmul_rn((float)sc[2 * pr], d), ml = __fmul_rn((float)mn[2 * pr], dmin);
+            const float sh = __fmul_rn((float)sc[2 * pr + 1], d),
+                        mh = __fmul_rn((float)mn[2 * pr + 1], dmin);
+            const uint32_t* wq = &q[c].x;
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+                float wl[4], wh[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t byte = (wq[wd] >> (8 * j)) & 0xFFu;
+                    wl[j] = __fsub_rn(__fmul_rn(small_int_f32(byte & 0xFu, 8388608.0f), sl), ml);
+                    wh[j] = __fsub_rn(__fmul_rn(small_int_f32(byte >> 4, 8388608.0f), sh), mh);
+                    if (rtz) {
+                        wl[j] = f16_round_trip_rtz(wl[j]);
+                        wh[j] = f16_round_trip_rtz(wh[j]);
+                    }
+                }
+                fma4<B>(acc, wl, xs, span, tile * 256 + 64 * pr + 16 * h + 4 * wd);
+                fma4<B>(acc, wh, xs, span, tile * 256 + 64 * pr + 32 + 16 * h + 4 * wd);
+            }
+        }
+    } else {
+        const int16_t* xq = reinterpret_cast<const int16_t*>(smem);
+        const int nblk = span / 32;
+        const float* sx = reinterpret_cast<const float*>(smem + (size_t)B * span * 2);
+        const int* sq = reinterpret_cast<const int*>(sx + B * nblk);
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            uint32_t lo[2][4], hi[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int wd = 0; wd < 4; ++wd) {
+                    uint32_t w = (&q[2 * pr + h].x)[wd];
+                    lo[h][wd] = w & 0x0F0F0F0Fu;
+                    hi[h][wd] = (w >> 4) & 0x0F0F0F0Fu;
+                }
+            const float dl = d * (float)sc[2 * pr], dh = d * (float)sc[2 * pr + 1];
+            const float ml = dmin * (float)mn[2 * pr], mh = dmin * (float)mn[2 * pr + 1];
+            const int jl = tile * 8 + 2 * pr, jh = jl + 1;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int4* xl = reinterpret_cast<const int4*>(xq + (size_t)b * span + jl * 32);
+                const int4* xh = reinterpret_cast<const int4*>(xq + (size_t)b * span + jh * 32);
+                int al = 0, ah = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    int4 L0 = xl[2 * h], L1 = xl[2 * h + 1];
+                    int4 H0 = xh[2 * h], H1 = xh[2 * h + 1];
+                    al = dp2a_lo_u8(L0.x, lo[h][0], al);
+                    al = dp2a_hi_u8(L0.y, lo[h][0], al);
+                    al = dp2a_lo_u8(L0.z, lo[h][1], al);
+                    al = dp2a_hi_u8(L0.w, lo[h][1], al);
+                    al = dp2a_lo_u8(L1.x, lo[h][2], al);
+                    al = dp2a_hi_u8(L1.y, lo[h][2], al);
+                    al = dp2a_lo_u8(L1.z, lo[h][3], al);
+                    al = dp2a_hi_u8(L1.w, lo[h][3], al);
+                    ah = dp2a_lo_u8(H0.x, hi[h][0], ah);
+                    ah = dp2a_hi_u8(H0.y, hi[h][0], ah);
+                    ah = dp2a_lo_u8(H0.z, hi[h][1], ah);
+                    ah = dp2a_hi_u8(H0.w, hi[h][1], ah);
+                    ah = dp2a_lo_u8(H1.x, hi[h][2], ah);
+                    ah = dp2a_hi_u8(H1.y, hi[h][2], ah);
+                    ah = dp2a_lo_u8(H1.z, hi[h][3], ah);
+                    ah = dp2a_hi_u8(H1.w, hi[h][3], ah);
+                }
+                const int bl = b * nblk + jl, bh = b * nblk + jh;
+                float v = sx[bl] * (dl * (float)al - ml * (float)sq[bl]) +
+                          sx[bh] * (dh * (float)ah - mh * (float)sq[bh]);
+                acc[b] += v;
+            }
+        }
+    }
+}
+
+// Epilogue --------------------------------------------------------------------
+template <int B>
+__device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t g, int lane,
+                                           const float (&v)[B]) {
+    const int64_t row = g * 32 + lane;
+    if (epi == EPI_SWIGLU) {
+        // lanes 0..15: gate rows, lanes 16..31: the matching up rows
+        const int64_t f = g * 16 + lane;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            float up = __shfl_down_sync(0xffffffffu, v[b], 16);
+            if (lane < 16 && b < p.batch && 2 * f < p.n) {
+                float gte = v[b];
+                float sig = 1.0f / (1.0f + expf(-gte));
+                p.y[b * p.y_ld + f] = (gte * sig) * up;
+            }
+        }
+        return;
+    }
+    if (row >= p.n) return;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        if (b >= p.batch) break;
+        float r = v[b];
+        if (epi == EPI_ADD) r = p.res[b * p.res_ld + row] + r;
+        p.y[b * p.y_ld + row] = r;
+    }
+}
+
+template <int FMT, int MODE, int B>
+__global__ void __launch_bounds__(128) qgemv_kernel(const GemvParams p, const int epi) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float red[4][B][32];
+    constexpr int CH = Fmt<FMT>::CH;
+    const int64_t g = blockIdx.x / p.ksplit;
+    const int s = blockIdx.x - (int)(g * p.ksplit);
+    const int t0 = s * p.tps;
+    const int t1 = (int)min((int64_t)p.ktiles, (int64_t)t0 + p.tps);
+    const int nt = t1 - t0;
+    const int span = nt * 256;
+    stage_x<FMT, MODE, B>(p, smem, (int64_t)t0 * 256, span);
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.0f;
+    const uint8_t* gbase = p.w + (g * p.ktiles + t0) * p.tile_bytes;
+    const bool rtz = p.rtz != 0;
+    for (int t = warp; t < nt; t += 4) {
+        const uint8_t* tp = gbase + (int64_t)t * p.tile_bytes;
+        const uint4 meta = ldg_stream(reinterpret_cast<const uint4*>(tp) + lane);
+        uint4 q[CH];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) q[c] = ldg_stream(reinterpret_cast<const uint4*>(tp + 512 + c * 512) + lane);
+        if (FMT == FMT_Q4_0)
+            consume_q4_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), smem, span, t, acc, rtz);
+        else if (FMT == FMT_Q8_0)
+            consume_q8_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[16]>(q), smem, span, t, acc, rtz);
+        else
+            consume_q4_k<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), smem, span, t, acc, rtz);
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) red[warp][b][lane] = acc[b];
+    __syncthreads();
+    if (warp != 0) return;
+    float v[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) v[b] = ((red[0][b][lane] + red[1][b][lane]) + red[2][b][lane]) + red[3][b][lane];
+    if (p.ksplit == 1) {
+        gemv_store<B>(p, epi, g, lane, v);
+        return;
+    }
+    // split-K: publish the partial, the last CTA of the row group reduces the
+    // partials in split order and runs the epilogue.
+    const int64_t row = g * 32 + lane;
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+        if (b < p.batch) p.partial[((int64_t)s * p.batch + b) * p.n_pad + row] = v[b];
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&p.counters[g], 1) == p.ksplit - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        float sum = 0.0f;
+        if (b < p.batch)
+            for (int s2 = 0; s2 < p.ksplit; ++s2)
+                sum += __ldcg(&p.partial[((int64_t)s2 * p.batch + b) * p.n_pad + row]);
+        v[b] = sum;
+    }
+    gemv_store<B>(p, epi, g, lane, v);
+    if (lane == 0) p.counters[g] = 0;
+}
+
+inline size_t gemv_smem_bytes(int mode, int bpad, int span) {
+    if (mode == MODE_F32) return (size_t)bpad * span * 4;
+    return (size_t)bpad * span * 2 + (size_t)bpad * (span / 32) * 8;
+}
+
+template <int FMT, int MODE, int B>
+void launch_qgemv_t(const GemvLaunch& a) {
+    const GemvPlan& pl = *a.plan;
+    GemvParams p;
+    p.w = static_cast<const uint8_t*>(a.w);
+    p.ktiles = a.L->ktiles();
+    p.tile_bytes = a.L->tile_bytes;
+    p.n = a.L->n;
+    p.n_pad = a.L->n_pad;
+    p.tps = pl.tps;
+    p.ksplit = pl.ksplit;
+    p.x = a.x;
+    p.x_f16 = a.x_f16 ? 1 : 0;
+    p.x_ld = a.x_ld;
+    p.k = a.L->k;
+    p.batch = a.batch;
+    p.y = a.y;
+    p.y_ld = a.y_ld;
+    p.res = a.res;
+    p.res_ld = a.res_ld;
+    p.partial = a.scratch.partial;
+    p.counters = a.scratch.counters;
+    p.rtz = a.rtz ? 1 : 0;
+    auto kern = qgemv_kernel<FMT, MODE, B>;
+    if (pl.smem > 48 * 1024)
+        BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+    const int64_t grid = a.L->groups() * pl.ksplit;
+    kern<<<(unsigned)grid, 128, pl.smem, a.s>>>(p, a.epi);
+    BC_LAUNCHED("qgemv_kernel");
+}
+
+template <int FMT>
+void launch_qgemv_fmt(const GemvLaunch& a) {
+    const int bp = a.plan->bpad;
+    if (a.mode == MODE_FAST) {
+        switch (bp) {
+            case 1: return launch_qgemv_t<FMT, MODE_FAST, 1>(a);
+            case 2: return launch_qgemv_t<FMT, MODE_FAST, 2>(a);
+            case 4: return launch_qgemv_t<FMT, MODE_FAST, 4>(a);
+            case 8: return launch_qgemv_t<FMT, MODE_FAST, 8>(a);
+            default: return launch_qgemv_t<FMT, MODE_FAST, 16>(a);
+        }
+    }
+    switch (bp) {
+        case 1: return launch_qgemv_t<FMT, MODE_F32, 1>(a);
+        case 2: return launch_qgemv_t<FMT, MODE_F32, 2>(a);
+        case 4: return launch_qgemv_t<FMT, MODE_F32, 4>(a);
+        case 8: return launch_qgemv_t<FMT, MODE_F32, 8>(a);
+        default: return launch_qgemv_t<FMT, MODE_F32, 16>(a);
+    }
+}
+
+}  // namespace bc

@@ -1,0 +1,75 @@
+// gemv_dispatch.cu -- split-K planning and format dispatch for the
+// dequant-GEMV kernels (gemv.cuh).
+#include <algorithm>
+
+#include "gemv.cuh"
+
+namespace bc {
+
+GemvPlan plan_qgemv(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
+    if (batch < 1 || batch > 16) invalid("quantized GEMV supports batch 1..16");
+    GemvPlan pl;
+    pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16;
+    const int64_t groups = L.groups(), ktiles = L.ktiles();
+    const size_t per_tile = gemv_smem_bytes(mode, pl.bpad, 256);
+    const int64_t tps_max = std::max<int64_t>(1, (int64_t)((96 * 1024) / per_tile));
+    // Enough CTAs for two per SM, but keep at least 4 tiles (one per warp)
+    // per CTA unless shared memory forces a finer split.
+    const int64_t target = 2 * (int64_t)(ctx ? ctx->sm_count : 148);
+    int64_t ks = (target + groups - 1) / groups;
+    ks = std::min<int64_t>(ks, std::max<int64_t>(1, ktiles / 4));
+    ks = std::max<int64_t>(ks, (ktiles + tps_max - 1) / tps_max);
+    ks = std::max<int64_t>(1, std::min<int64_t>(ks, ktiles));
+    int64_t tps = (ktiles + ks - 1) / ks;
+    ks = (ktiles + tps - 1) / tps;
+    pl.ksplit = (int)ks;
+    pl.tps = (int)tps;
+    pl.smem = gemv_smem_bytes(mode, pl.bpad, (int)tps * 256);
+    return pl;
+}
+
+void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16,
+                  int64_t x_ld, int batch, float* y, int64_t y_ld, int epi, const float* res,
+                  int64_t res_ld, int mode, bool rtz, const GemvScratch& scratch, cudaStream_t s) {
+    if (plan.ksplit > 1) {
+        if (!scratch.partial || !scratch.counters ||
+            scratch.partial_floats < (size_t)plan.ksplit * batch * L.n_pad ||
+            scratch.counter_count < L.groups())
+            invalid("split-K GEMV launched without enough scratch");
+    }
+    GemvLaunch a{&plan, &L, w, x, x_f16, x_ld, batch, y, y_ld, epi, res, res_ld, mode, rtz, scratch, s};
+    switch (L.dtype) {
+        case BEACON_CUDA_DTYPE_Q4_0: return launch_qgemv_q4_0(a);
+        case BEACON_CUDA_DTYPE_Q8_0: return launch_qgemv_q8_0(a);
+        case BEACON_CUDA_DTYPE_Q4_K: return launch_qgemv_q4_k(a);
+        default: fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized GEMV: unsupported block type");
+    }
+}
+
+// Prefill-sized matmul through the GEMV in 16-row chunks (each chunk streams
+// the weight once). Numerics follow the context's mode exactly.
+void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTensor* w, const void* x, bool x_f16,
+                   int64_t rows, float* out, int numerics) {
+    const int mode = numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32;
+    const bool rtz = numerics == BEACON_CUDA_NUMERICS_REF_RTZ;
+    const QLayout& L = w->q;
+    const size_t eb = x_f16 ? 2 : 4;
+    for (int64_t r0 = 0; r0 < rows; r0 += 16) {
+        const int b = (int)std::min<int64_t>(16, rows - r0);
+        GemvPlan pl = plan_qgemv(ctx, L, b, mode);
+        GemvScratch sc;
+        if (pl.ksplit > 1) {
+            size_t pf = (size_t)pl.ksplit * b * L.n_pad;
+            size_t coff = (pf * 4 + 255) / 256 * 256;
+            uint8_t* base = static_cast<uint8_t*>(ctx->ws.get(coff + (size_t)L.groups() * 4, s));
+            sc.partial = reinterpret_cast<float*>(base);
+            sc.partial_floats = pf;
+            sc.counters = reinterpret_cast<int*>(base + coff);
+            sc.counter_count = L.groups();
+        }
+        launch_qgemv(pl, L, w->data(), static_cast<const uint8_t*>(x) + (size_t)r0 * L.k * eb, x_f16, L.k, b,
+                     out + r0 * L.n, L.n, EPI_STORE, nullptr, 0, mode, rtz, sc, s);
+    }
+}
+
+}  // namespace bc

@@ -1,0 +1,82 @@
+// kernels.h -- host-side launchers shared between translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "internal.h"
+
+namespace bc {
+
+enum GemvMode { MODE_FAST = 0, MODE_F32 = 1 };
+enum GemvEpilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+
+// Scratch for split-K GEMV: partial sums and one arrival counter per 32-row
+// group. Counters must be zero before the first launch; every launch leaves
+// them at zero again.
+struct GemvScratch {
+    float* partial = nullptr;
+    int* counters = nullptr;
+    size_t partial_floats = 0;
+    int64_t counter_count = 0;
+};
+
+struct GemvPlan {
+    int ksplit = 1;
+    int tps = 1;  // 256-column tiles per CTA
+    int bpad = 1;
+    size_t smem = 0;
+};
+
+// y[b, n] (+)= sum_k W[n, k] x[b, k] for a tiled quantized W (QLayout).
+//  x: batch rows of x_ld elements, f32 or f16. y: f32, row stride y_ld.
+//  EPI_ADD: y = res + W x.  EPI_SWIGLU: rows of W interleave gate/up per
+//  16-row half group; y has n/2 columns = silu(gate) * up.
+GemvPlan plan_qgemv(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode);
+void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const void* x,
+                  bool x_f16, int64_t x_ld, int batch, float* y, int64_t y_ld, int epi,
+                  const float* res, int64_t res_ld, int mode, bool rtz, const GemvScratch& scratch,
+                  cudaStream_t s);
+
+// Per-format instantiation entry points (gemv_<fmt>.cu).
+struct GemvLaunch {
+    const GemvPlan* plan;
+    const QLayout* L;
+    const void* w;
+    const void* x;
+    bool x_f16;
+    int64_t x_ld;
+    int batch;
+    float* y;
+    int64_t y_ld;
+    int epi;
+    const float* res;
+    int64_t res_ld;
+    int mode;
+    bool rtz;
+    GemvScratch scratch;
+    cudaStream_t s;
+};
+void launch_qgemv_q4_0(const GemvLaunch& a);
+void launch_qgemv_q8_0(const GemvLaunch& a);
+void launch_qgemv_q4_k(const GemvLaunch& a);
+
+// Quantized layout kernels (quant.cu). row_map (device, one entry per tiled
+// row, optional): raw row to copy, -1 = zero row, -2 = leave the row as is.
+void launch_repack(const QLayout& L, const uint8_t* raw, int nibble_order, uint8_t* tiled,
+                   const int64_t* row_map, cudaStream_t s);
+void launch_dequant_f16(const QLayout& L, const uint8_t* tiled, uint16_t* out, cudaStream_t s);
+void launch_quantize(int32_t dtype, const float* x, int64_t n_rows, int64_t k, int nibble_order,
+                     uint8_t* raw, cudaStream_t s);
+
+// Prefill-sized quantized matmul (rows > 16): out[rows, N] = x @ W^T.
+void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTensor* w, const void* x,
+                   bool x_f16, int64_t rows, float* out, int numerics);
+
+// Tensor parallelism (comm.cu).
+void comm_destroy(BeaconCudaContext* ctx);
+void comm_all_reduce_sum(BeaconCudaContext* ctx, float* buf, size_t count, cudaStream_t s);
+void comm_all_gather(BeaconCudaContext* ctx, const float* send, float* recv, size_t count, cudaStream_t s);
+
+}  // namespace bc

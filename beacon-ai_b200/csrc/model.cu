@@ -1,0 +1,949 @@
+// model.cu -- fused Llama-style decoder runtime on one GPU (or one tensor-
+// parallel rank): the op sequence of Engine<B>::forward (engine.rs:190-456)
+// with the seven projections per layer and lm_head served by the dequant-GEMV
+// kernels, the decode step captured once per batch size in a CUDA graph.
+//
+// Per layer (decode, B sequences, one token each):
+//   rms_norm(h)                       -> xn
+//   [Wq;Wk;Wv] xn          (one GEMV) -> qkv
+//   rope(q,k) + K/V cache write       -> q, cache[b][pos]
+//   split-K decode attention          -> attn
+//   h += Wo attn           (GEMV, residual add fused; TP: + all-reduce)
+//   rms_norm(h)                       -> xn
+//   silu(Wg xn) * (Wu xn)  (one GEMV over interleaved gate/up rows)
+//   h += Wd act            (GEMV, residual add fused; TP: + all-reduce)
+// then rms_norm, lm_head GEMV (vocab-split under TP, all-gathered) and
+// greedy argmax with the reference's tie rule (sampling.rs:60-66).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "attention.h"
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+
+namespace bc {
+
+namespace {
+
+constexpr int kPrefillChunk = 512;
+
+// --- small kernels ------------------------------------------------------------
+
+__device__ __forceinline__ int read_pos(const int* pos_ptr, int pos_imm) { return pos_ptr ? *pos_ptr : pos_imm; }
+
+// h[row] = E[tok[row]] (f32). Out-of-range ids write zeros and raise *err.
+__global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hid, const int32_t* tok, float* h,
+                             int* err) {
+    const int row = blockIdx.x;
+    const int32_t t = tok[row];
+    const bool ok = t >= 0 && t < vocab;
+    if (!ok && threadIdx.x == 0) atomicExch(err, 1);
+    for (int64_t i = threadIdx.x; i < hid; i += blockDim.x) {
+        float v = 0.0f;
+        if (ok) v = e_f16 ? __half2float(static_cast<const __half*>(E)[(int64_t)t * hid + i])
+                          : static_cast<const float*>(E)[(int64_t)t * hid + i];
+        h[(int64_t)row * hid + i] = v;
+    }
+}
+
+// ops.rs:77-93 per row; w is f32
+__global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, int64_t d, float eps) {
+    __shared__ float sh[32];
+    const int64_t row = blockIdx.x;
+    const float* xr = x + row * d;
+    float ss = 0.0f;
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += sh[i];
+    const float inv = 1.0f / sqrtf(t / (float)d + eps);
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) out[row * d + i] = xr[i] * inv * w[i];
+}
+
+// cos/sin table [max_ctx][D/2] with the CPU formula (ops.rs:131-135)
+__global__ void rope_table_kernel(float* cs, float* sn, int max_ctx, int d, float theta) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int half = d / 2;
+    if (idx >= (int64_t)max_ctx * half) return;
+    const int p = (int)(idx / half), i = (int)(idx % half);
+    const float freq = 1.0f / powf(theta, (float)(2 * i) / (float)d);
+    const float angle = (float)p * freq;
+    float s, c;
+    sincosf(angle, &s, &c);
+    cs[idx] = c;
+    sn[idx] = s;
+}
+
+// qkv [rows][qd + 2 kd] -> q [rows][qd] (roped), K/V cache rows (k roped).
+// Row r is sequence (seq0 + r*seq_step) at position pos + r*pos_step.
+template <typename KV>
+__global__ void qkv_post_kernel(const float* qkv, float* q, KV* kc, KV* vc, const float* cs, const float* sn,
+                                int rows, int qd, int kd, int d, int64_t cache_sb, const int* pos_ptr, int pos_imm,
+                                int pos_step, int seq_step) {
+    const int r = blockIdx.y;
+    const int pos0 = read_pos(pos_ptr, pos_imm);
+    const int pos = pos0 + r * pos_step;
+    const int seq = r * seq_step;
+    const int qkvn = qd + 2 * kd;
+    const float* src = qkv + (int64_t)r * qkvn;
+    const int half = d / 2;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < qd / 2 + kd / 2 + kd / 2; j += gridDim.x * blockDim.x) {
+        if (j < qd / 2) {  // q pair
+            const int e = 2 * j, i = (e % d) / 2;
+            const float c = cs[(int64_t)pos * half + i], s = sn[(int64_t)pos * half + i];
+            const float x0 = src[e], x1 = src[e + 1];
+            q[(int64_t)r * qd + e] = x0 * c - x1 * s;
+            q[(int64_t)r * qd + e + 1] = x0 * s + x1 * c;
+        } else if (j < qd / 2 + kd / 2) {  // k pair
+            const int e = 2 * (j - qd / 2), i = (e % d) / 2;
+            const float c = cs[(int64_t)pos * half + i], s = sn[(int64_t)pos * half + i];
+            const float x0 = src[qd + e], x1 = src[qd + e + 1];
+            KV* dst = kc + (int64_t)seq * cache_sb + (int64_t)pos * kd + e;
+            dst[0] = (KV)(x0 * c - x1 * s);
+            dst[1] = (KV)(x0 * s + x1 * c);
+        } else {  // v pair
+            const int e = 2 * (j - qd / 2 - kd / 2);
+            KV* dst = vc + (int64_t)seq * cache_sb + (int64_t)pos * kd + e;
+            dst[0] = (KV)src[qd + kd + e];
+            dst[1] = (KV)src[qd + kd + e + 1];
+        }
+    }
+}
+
+// Greedy argmax per row (rule of sampling.rs:60-66, see ops.cu). logits are
+// [rows][n] or, with parts > 1, [parts][rows][n/parts] (all-gathered shards).
+__global__ void argmax_rows_kernel(const float* x, int64_t n, int parts, int rows, int32_t* out, int32_t* out2) {
+    __shared__ int64_t shi[32];
+    __shared__ float shv[32];
+    const int row = blockIdx.x;
+    const int64_t per = n / parts;
+    auto at = [&](int64_t i) -> float {
+        const int64_t p = i / per, j = i - p * per;
+        return x[(p * rows + row) * per + j];
+    };
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    int64_t last_nan = -1;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+        if (isnan(at(i))) last_nan = i;
+    for (int o = 16; o; o >>= 1) last_nan = max(last_nan, __shfl_xor_sync(0xffffffffu, last_nan, o));
+    if (l == 0) shi[w] = last_nan;
+    __syncthreads();
+    last_nan = -1;
+    for (int i = 0; i < nw; ++i) last_nan = max(last_nan, shi[i]);
+    __syncthreads();
+    int64_t result;
+    if (last_nan == n - 1) {
+        result = n - 1;
+    } else {
+        float bv = -INFINITY;
+        int64_t bi = -1;
+        for (int64_t i = last_nan + 1 + threadIdx.x; i < n; i += blockDim.x) {
+            float c = at(i);
+            if (bi < 0 || c > bv || (c == bv && i > bi)) {
+                bv = c;
+                bi = i;
+            }
+        }
+        for (int o = 16; o; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (l == 0) {
+            shv[w] = bv;
+            shi[w] = bi;
+        }
+        __syncthreads();
+        bv = -INFINITY;
+        bi = -1;
+        for (int i = 0; i < nw; ++i)
+            if (shi[i] >= 0 && (bi < 0 || shv[i] > bv || (shv[i] == bv && shi[i] > bi))) {
+                bv = shv[i];
+                bi = shi[i];
+            }
+        result = bi;
+    }
+    if (threadIdx.x == 0) {
+        out[row] = (int32_t)result;
+        if (out2) out2[row] = (int32_t)result;
+    }
+}
+
+// [parts][rows][per] -> [rows][parts*per]
+__global__ void unshard_kernel(const float* in, float* out, int parts, int rows, int64_t per) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n = (int64_t)parts * rows * per;
+    if (i >= n) return;
+    const int64_t p = i / (rows * per), r = (i / per) % rows, j = i % per;
+    out[r * (parts * per) + p * per + j] = in[i];
+}
+
+__global__ void advance_kernel(int* pos) { *pos += 1; }
+
+inline unsigned cdiv(int64_t a, int64_t b) { return (unsigned)std::max<int64_t>(1, (a + b - 1) / b); }
+
+}  // namespace
+
+struct LayerW {
+    std::unique_ptr<DeviceBuffer> attn_norm, ffn_norm;
+    std::unique_ptr<DeviceBuffer> wqkv, wo, wgu, wd;
+    std::unique_ptr<DeviceBuffer> kc, vc;
+    unsigned set = 0;
+};
+
+}  // namespace bc
+
+struct BeaconCudaModel {
+    BeaconCudaContext* ctx = nullptr;
+    BeaconCudaModelConfig cfg{};
+    int tp = 1, rank = 0;
+    int h_loc = 0, kv_loc = 0, f_loc = 0;
+    int64_t v_loc = 0, v0 = 0, qd = 0, kd = 0, qkv_n = 0;
+    int32_t wdtype = -1;
+    bc::QLayout Lqkv, Lo, Lgu, Ld, Llm;
+    std::vector<bc::LayerW> layers;
+    std::unique_ptr<bc::DeviceBuffer> embed, final_norm, wlm, rope_cs, rope_sn;
+    int32_t embed_dtype = BEACON_CUDA_DTYPE_F16;
+    unsigned global_set = 0;
+    int max_rows = 1;
+    // activations
+    std::unique_ptr<bc::DeviceBuffer> act;
+    float *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *ffn = nullptr;
+    float *logits_loc = nullptr, *logits_all = nullptr, *logits = nullptr;
+    int32_t *tok = nullptr, *next = nullptr;
+    int* pos_dev = nullptr;
+    int* err_dev = nullptr;
+    // scratch
+    bc::GemvScratch gsc;
+    std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
+    int attn_nsplit = 1;
+    float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
+    // host staging (pinned)
+    int32_t* h_stage = nullptr;  // [0] = position, [1..] tokens
+    int32_t* h_next = nullptr;
+    // graphs: key = batch * 2 + autoregressive
+    std::map<int, cudaGraphExec_t> graphs;
+    ~BeaconCudaModel();
+};
+
+namespace bc {
+namespace {
+
+int gemv_mode(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32; }
+bool gemv_rtz(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_NUMERICS_REF_RTZ; }
+
+// y = W x over `rows` rows of x, in chunks of 16 rows (the GEMV batch limit).
+void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
+            int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s) {
+    for (int r0 = 0; r0 < rows; r0 += 16) {
+        const int b = std::min(16, rows - r0);
+        GemvPlan pl = plan_qgemv(m->ctx, L, b, gemv_mode(m));
+        launch_qgemv(pl, L, w, x + (int64_t)r0 * x_ld, false, x_ld, b, y + (int64_t)r0 * y_ld, y_ld, epi,
+                     res ? res + (int64_t)r0 * res_ld : nullptr, res_ld, gemv_mode(m), gemv_rtz(m), m->gsc, s);
+    }
+}
+
+void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int rows, cudaStream_t s) {
+    rmsnorm_rows_kernel<<<rows, 256, 0, s>>>(x, w, out, m->cfg.hidden_size, m->cfg.rms_norm_eps);
+    BC_LAUNCHED("rmsnorm_rows_kernel");
+}
+
+// One pass of the decoder over `rows` rows that are either B sequences at
+// one position (decode) or consecutive tokens of sequence 0 (prefill chunk).
+// pos_ptr != nullptr: positions come from device memory (graph capture).
+void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, int pos_imm, cudaStream_t s) {
+    const auto& c = m->cfg;
+    const int64_t hid = c.hidden_size;
+    const int D = c.head_dim;
+    const bool f16kv = c.kv_dtype == BEACON_CUDA_DTYPE_F16;
+    const int64_t cache_sb = (int64_t)c.max_context * m->kd;
+    for (int li = 0; li < c.num_layers; ++li) {
+        LayerW& L = m->layers[li];
+        rmsnorm(m, m->h, static_cast<const float*>(L.attn_norm->ptr), m->xn, rows, s);
+        linear(m, m->Lqkv, L.wqkv->ptr, m->xn, hid, rows, m->qkv, m->qkv_n, EPI_STORE, nullptr, 0, s);
+        {
+            dim3 grid(cdiv(m->qd / 2 + m->kd, 256), rows);
+            const int pos_step = decode ? 0 : 1, seq_step = decode ? 1 : 0;
+            if (f16kv)
+                qkv_post_kernel<__half><<<grid, 256, 0, s>>>(
+                    m->qkv, m->q, static_cast<__half*>(L.kc->ptr), static_cast<__half*>(L.vc->ptr),
+                    static_cast<const float*>(m->rope_cs->ptr), static_cast<const float*>(m->rope_sn->ptr), rows,
+                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step);
+            else
+                qkv_post_kernel<float><<<grid, 256, 0, s>>>(
+                    m->qkv, m->q, static_cast<float*>(L.kc->ptr), static_cast<float*>(L.vc->ptr),
+                    static_cast<const float*>(m->rope_cs->ptr), static_cast<const float*>(m->rope_sn->ptr), rows,
+                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step);
+            BC_LAUNCHED("qkv_post_kernel");
+        }
+        const float scale = 1.0f / sqrtf((float)D);  // engine.rs:415
+        if (decode) {
+            DecodeAttnArgs a{};
+            a.q = m->q;
+            a.k_cache = L.kc->ptr;
+            a.v_cache = L.vc->ptr;
+            a.kv_f16 = f16kv;
+            a.cache_sb = cache_sb;
+            a.batch = rows;
+            a.heads = m->h_loc;
+            a.kv_heads = m->kv_loc;
+            a.d = D;
+            a.pos_ptr = pos_ptr;
+            a.kv_len = pos_imm + 1;
+            a.scale = scale;
+            a.nsplit = m->attn_nsplit;
+            a.part_acc = m->pacc;
+            a.part_m = m->pm;
+            a.part_l = m->pl;
+            a.out = m->attn;
+            launch_decode_attention(a, s);
+        } else {
+            AttnRowsArgs a{};
+            a.q = m->q;
+            a.q_f16 = 0;
+            a.k = L.kc->ptr;
+            a.v = L.vc->ptr;
+            a.kv_f16 = f16kv;
+            a.out = m->attn;
+            a.batch = 1;
+            a.heads = m->h_loc;
+            a.kv_heads = m->kv_loc;
+            a.sq = rows;
+            a.skv = pos_imm + rows;
+            a.d = D;
+            a.scale = scale;
+            a.causal = c.causal_prefill && rows > 1 ? 1 : 0;
+            a.q_sb = 0;
+            a.q_sh = D;
+            a.q_ss = m->qd;
+            a.kv_sb = 0;
+            a.kv_sh = D;
+            a.kv_ss = m->kd;
+            a.o_sb = 0;
+            a.o_sh = D;
+            a.o_ss = m->qd;
+            launch_attention_rows(a, s);
+        }
+        // h = h + Wo attn ; under TP only rank 0 adds the residual, then sum
+        const bool r0 = m->rank == 0;
+        linear(m, m->Lo, L.wo->ptr, m->attn, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE, r0 ? m->h : nullptr,
+               hid, s);
+        comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
+        rmsnorm(m, m->h, static_cast<const float*>(L.ffn_norm->ptr), m->xn, rows, s);
+        linear(m, m->Lgu, L.wgu->ptr, m->xn, hid, rows, m->ffn, m->f_loc, EPI_SWIGLU, nullptr, 0, s);
+        linear(m, m->Ld, L.wd->ptr, m->ffn, m->f_loc, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE, r0 ? m->h : nullptr,
+               hid, s);
+        comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
+    }
+    // final norm + lm_head (engine.rs:230-234)
+    rmsnorm(m, m->h, static_cast<const float*>(m->final_norm->ptr), m->xn, rows, s);
+    linear(m, m->Llm, m->wlm->ptr, m->xn, hid, rows, m->logits_loc, m->v_loc, EPI_STORE, nullptr, 0, s);
+    if (m->tp > 1) {
+        comm_all_gather(m->ctx, m->logits_loc, m->logits_all, (size_t)rows * m->v_loc, s);
+    }
+}
+
+// logits [rows][V] (unsharded) and argmax -> next (and tok, for the next step)
+void finish_logits(BeaconCudaModel* m, int rows, bool need_full_logits, bool feed_back, cudaStream_t s) {
+    const int64_t V = m->cfg.vocab_size;
+    const float* src = m->tp > 1 ? m->logits_all : m->logits_loc;
+    argmax_rows_kernel<<<rows, 256, 0, s>>>(src, m->v_loc * m->tp, m->tp, rows, m->next, feed_back ? m->tok : nullptr);
+    BC_LAUNCHED("argmax_rows_kernel");
+    if (need_full_logits && m->tp > 1) {
+        unshard_kernel<<<cdiv((int64_t)rows * m->v_loc * m->tp, 256), 256, 0, s>>>(m->logits_all, m->logits, m->tp, rows,
+                                                                                    m->v_loc);
+        BC_LAUNCHED("unshard_kernel");
+    }
+    (void)V;
+}
+
+float* full_logits(BeaconCudaModel* m) { return m->tp > 1 ? m->logits : m->logits_loc; }
+
+void decode_body(BeaconCudaModel* m, int batch, bool autoregressive, cudaStream_t s) {
+    embed_kernel<<<batch, 256, 0, s>>>(m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, m->cfg.vocab_size,
+                                       m->cfg.hidden_size, m->tok, m->h, m->err_dev);
+    BC_LAUNCHED("embed_kernel");
+    run_layers(m, batch, true, m->pos_dev, 0, s);
+    finish_logits(m, batch, m->tp > 1, autoregressive, s);
+    if (autoregressive) {
+        advance_kernel<<<1, 1, 0, s>>>(m->pos_dev);
+        BC_LAUNCHED("advance_kernel");
+    }
+}
+
+void check_ready(const BeaconCudaModel* m) {
+    const unsigned layer_all = (1u << 9) - 1;
+    if ((m->global_set & 7u) != 7u) invalid("model: embed / final_norm / lm_head not set");
+    for (size_t i = 0; i < m->layers.size(); ++i)
+        if (m->layers[i].set != layer_all) invalid("model: layer " + std::to_string(i) + " has unset weights");
+}
+
+void check_err(BeaconCudaModel* m, cudaStream_t s) {
+    int herr = 0;
+    BC_CUDA(cudaMemcpyAsync(&herr, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s));
+    BC_CUDA(cudaStreamSynchronize(s));
+    if (herr) {
+        BC_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), s));
+        shape_err("token id out of range for the vocabulary");
+    }
+}
+
+// Copy the raw GGUF bytes of rows [r0, r0+nr) and columns [c0, c0+nc) of a
+// [N, K] tensor into a packed device buffer.
+std::unique_ptr<DeviceBuffer> slice_raw(const void* data, bool on_device, int32_t dtype, int64_t K, int64_t r0,
+                                        int64_t nr, int64_t c0, int64_t nc, cudaStream_t s) {
+    const int64_t bs = block_size(dtype), bb = block_bytes(dtype);
+    if (c0 % bs || nc % bs) shape_err("tensor-parallel shard is not a whole number of blocks");
+    const int64_t row_bytes = K / bs * bb, off = c0 / bs * bb, w = nc / bs * bb;
+    auto buf = std::make_unique<DeviceBuffer>((size_t)(nr * w));
+    const uint8_t* src = static_cast<const uint8_t*>(data) + r0 * row_bytes + off;
+    BC_CUDA(cudaMemcpy2DAsync(buf->ptr, (size_t)w, src, (size_t)row_bytes, (size_t)w, (size_t)nr,
+                              on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+    return buf;
+}
+
+void repack_into(BeaconCudaModel* m, const QLayout& L, void* dst, const void* raw, int nibble,
+                 const std::vector<int64_t>& row_map, cudaStream_t s) {
+    DeviceBuffer map((size_t)L.n_pad * sizeof(int64_t));
+    BC_CUDA(cudaMemcpyAsync(map.ptr, row_map.data(), row_map.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    launch_repack(L, static_cast<const uint8_t*>(raw), nibble, static_cast<uint8_t*>(dst),
+                  static_cast<const int64_t*>(map.ptr), s);
+    BC_CUDA(cudaStreamSynchronize(s));
+    (void)m;
+}
+
+std::unique_ptr<DeviceBuffer> upload_plain_f32(const void* data, bool on_device, int32_t dtype, int64_t n,
+                                               cudaStream_t s) {
+    // norm weights -> f32 on the device
+    auto out = std::make_unique<DeviceBuffer>((size_t)n * 4);
+    std::vector<float> host((size_t)n);
+    if (dtype != BEACON_CUDA_DTYPE_F32 && dtype != BEACON_CUDA_DTYPE_F16)
+        fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "norm weights must be F32 or F16");
+    const size_t eb = dtype == BEACON_CUDA_DTYPE_F32 ? 4 : 2;
+    std::vector<uint8_t> raw((size_t)n * eb);
+    if (on_device)
+        BC_CUDA(cudaMemcpy(raw.data(), data, raw.size(), cudaMemcpyDeviceToHost));
+    else
+        std::memcpy(raw.data(), data, raw.size());
+    for (int64_t i = 0; i < n; ++i) {
+        if (eb == 4) {
+            std::memcpy(&host[i], &raw[4 * i], 4);
+        } else {
+            uint16_t hbits;
+            std::memcpy(&hbits, &raw[2 * i], 2);
+            uint32_t b = f16_to_f32_bits(hbits);
+            std::memcpy(&host[i], &b, 4);
+        }
+    }
+    BC_CUDA(cudaMemcpyAsync(out->ptr, host.data(), (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    BC_CUDA(cudaStreamSynchronize(s));
+    return out;
+}
+
+void release_graphs(BeaconCudaModel* m) {
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    m->graphs.clear();
+}
+
+}  // namespace
+}  // namespace bc
+
+BeaconCudaModel::~BeaconCudaModel() {
+    bc::release_graphs(this);
+    if (h_stage) cudaFreeHost(h_stage);
+    if (h_next) cudaFreeHost(h_next);
+}
+
+using namespace bc;
+
+extern "C" {
+
+int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelConfig* cfg, BeaconCudaModel** out) {
+    return guard([&]() -> int32_t {
+        require(ctx && cfg && out, "model_create: null argument");
+        set_device(ctx);
+        const BeaconCudaModelConfig& c = *cfg;
+        if (c.vocab_size <= 0 || c.hidden_size <= 0 || c.num_layers <= 0 || c.num_heads <= 0 ||
+            c.num_kv_heads <= 0 || c.head_dim <= 0 || c.intermediate_size <= 0 || c.max_context <= 0 ||
+            c.max_batch <= 0)
+            invalid("model_create: every dimension must be positive");
+        if (c.num_heads % c.num_kv_heads) shape_err("model_create: num_heads % num_kv_heads != 0");
+        if (c.num_heads * c.head_dim != c.hidden_size) shape_err("model_create: num_heads * head_dim != hidden_size");
+        if (c.head_dim % 32) shape_err("model_create: head_dim must be a multiple of 32");
+        if (c.kv_dtype != BEACON_CUDA_DTYPE_F16 && c.kv_dtype != BEACON_CUDA_DTYPE_F32)
+            fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "model_create: kv_dtype must be F16 or F32");
+        if (c.numerics < 0 || c.numerics > 2) invalid("model_create: unknown numerics");
+        const int tp = std::max(1, c.tp_size);
+        if (c.tp_rank < 0 || c.tp_rank >= tp) invalid("model_create: bad tp_rank");
+        if (tp != ctx->nranks || (tp > 1 && c.tp_rank != ctx->rank))
+            invalid("model_create: tp_size/tp_rank must match the context's communicator");
+        if (c.num_kv_heads % tp || c.intermediate_size % tp || c.vocab_size % tp)
+            shape_err("model_create: kv heads, intermediate size and vocab must divide by tp_size");
+        auto m = std::make_unique<BeaconCudaModel>();
+        m->ctx = ctx;
+        m->cfg = c;
+        m->tp = tp;
+        m->rank = c.tp_rank;
+        m->h_loc = c.num_heads / tp;
+        m->kv_loc = c.num_kv_heads / tp;
+        m->f_loc = c.intermediate_size / tp;
+        m->v_loc = c.vocab_size / tp;
+        m->v0 = m->v_loc * m->rank;
+        m->qd = (int64_t)m->h_loc * c.head_dim;
+        m->kd = (int64_t)m->kv_loc * c.head_dim;
+        m->qkv_n = m->qd + 2 * m->kd;
+        if (!decode_attention_supported(c.head_dim, c.num_heads / c.num_kv_heads))
+            shape_err("model_create: head_dim must be 64 or 128 and heads/kv_heads in {1, 2, 4, 8}");
+        m->layers.resize(c.num_layers);
+        // KV caches [max_batch][max_ctx][kv_loc][D]
+        const size_t kvb = (size_t)c.max_batch * c.max_context * m->kd * (c.kv_dtype == BEACON_CUDA_DTYPE_F16 ? 2 : 4);
+        for (auto& L : m->layers) {
+            L.kc = std::make_unique<DeviceBuffer>(kvb);
+            L.vc = std::make_unique<DeviceBuffer>(kvb);
+            BC_CUDA(cudaMemset(L.kc->ptr, 0, kvb));
+            BC_CUDA(cudaMemset(L.vc->ptr, 0, kvb));
+        }
+        // rope table
+        const int half = c.head_dim / 2;
+        m->rope_cs = std::make_unique<DeviceBuffer>((size_t)c.max_context * half * 4);
+        m->rope_sn = std::make_unique<DeviceBuffer>((size_t)c.max_context * half * 4);
+        rope_table_kernel<<<cdiv((int64_t)c.max_context * half, 256), 256>>>(
+            static_cast<float*>(m->rope_cs->ptr), static_cast<float*>(m->rope_sn->ptr), c.max_context, c.head_dim,
+            c.rope_theta);
+        BC_LAUNCHED("rope_table_kernel");
+        // activations
+        m->max_rows = std::max(c.max_batch, std::min(c.max_context, kPrefillChunk));
+        const int64_t R = m->max_rows;
+        const int64_t Vt = (int64_t)m->v_loc * tp;
+        size_t floats = 0;
+        auto carve = [&](int64_t n) {
+            size_t off = floats;
+            floats += (size_t)((n + 63) / 64 * 64);
+            return off;
+        };
+        size_t o_h = carve(R * c.hidden_size), o_xn = carve(R * c.hidden_size), o_qkv = carve(R * m->qkv_n),
+               o_q = carve(R * m->qd), o_attn = carve(R * m->qd), o_ffn = carve(R * m->f_loc),
+               o_ll = carve(R * m->v_loc), o_la = carve(tp > 1 ? R * Vt : 64), o_lg = carve(tp > 1 ? R * Vt : 64),
+               o_tok = carve(R), o_next = carve(R), o_pos = carve(64);
+        m->act = std::make_unique<DeviceBuffer>(floats * 4);
+        BC_CUDA(cudaMemset(m->act->ptr, 0, floats * 4));
+        float* base = static_cast<float*>(m->act->ptr);
+        m->h = base + o_h;
+        m->xn = base + o_xn;
+        m->qkv = base + o_qkv;
+        m->q = base + o_q;
+        m->attn = base + o_attn;
+        m->ffn = base + o_ffn;
+        m->logits_loc = base + o_ll;
+        m->logits_all = base + o_la;
+        m->logits = base + o_lg;
+        m->tok = reinterpret_cast<int32_t*>(base + o_tok);
+        m->next = reinterpret_cast<int32_t*>(base + o_next);
+        m->pos_dev = reinterpret_cast<int*>(base + o_pos);
+        m->err_dev = m->pos_dev + 16;
+        // attention split scratch (decode)
+        m->attn_nsplit = plan_decode_splits(c.max_batch, m->kv_loc, c.max_context, ctx->sm_count, 64);
+        const size_t pa = (size_t)c.max_batch * m->h_loc * m->attn_nsplit;
+        m->attn_buf = std::make_unique<DeviceBuffer>((pa * c.head_dim + 2 * pa) * 4);
+        m->pacc = static_cast<float*>(m->attn_buf->ptr);
+        m->pm = m->pacc + pa * c.head_dim;
+        m->pl = m->pm + pa;
+        BC_CUDA(cudaMallocHost(&m->h_stage, (size_t)(R + 1) * 4));
+        BC_CUDA(cudaMallocHost(&m->h_next, (size_t)R * 4));
+        BC_CUDA(cudaDeviceSynchronize());
+        *out = m.release();
+        return BEACON_CUDA_OK;
+    });
+}
+
+void beacon_cuda_model_destroy(BeaconCudaModel* model) {
+    if (!model) return;
+    cudaSetDevice(model->ctx->device);
+    cudaDeviceSynchronize();
+    delete model;
+}
+
+int32_t beacon_cuda_model_set_weight(BeaconCudaModel* m, int32_t layer, int32_t slot, const void* data, int32_t dtype,
+                                     int32_t nibble_order, int32_t on_device) {
+    return guard([&]() -> int32_t {
+        require(m && data, "model_set_weight: null argument");
+        set_device(m->ctx);
+        release_graphs(m);
+        const auto& c = m->cfg;
+        cudaStream_t s = m->ctx->internal;
+        const bool dev = on_device != 0;
+        const int64_t H = c.hidden_size, D = c.head_dim;
+        auto quant_check = [&]() {
+            if (!is_quantized(dtype)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "linear weights must be GGUF blocks");
+            if (m->wdtype < 0) {
+                m->wdtype = dtype;
+            }
+        };
+        auto identity_map = [](const QLayout& L, int64_t r0, int64_t nr, int64_t src0) {
+            std::vector<int64_t> map((size_t)L.n_pad, -2);
+            for (int64_t r = 0; r < nr; ++r) map[(size_t)(r0 + r)] = src0 + r;
+            return map;
+        };
+        if (slot == BEACON_CUDA_W_EMBED) {
+            if (dtype != BEACON_CUDA_DTYPE_F16 && dtype != BEACON_CUDA_DTYPE_F32)
+                fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "embedding must be F16 or F32");
+            const size_t n = (size_t)c.vocab_size * H * (dtype == BEACON_CUDA_DTYPE_F16 ? 2 : 4);
+            m->embed = std::make_unique<DeviceBuffer>(n);
+            BC_CUDA(cudaMemcpy(m->embed->ptr, data, n, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+            m->embed_dtype = dtype;
+            m->global_set |= 1u;
+            return BEACON_CUDA_OK;
+        }
+        if (slot == BEACON_CUDA_W_FINAL_NORM) {
+            m->final_norm = upload_plain_f32(data, dev, dtype, H, s);
+            m->global_set |= 2u;
+            return BEACON_CUDA_OK;
+        }
+        if (slot == BEACON_CUDA_W_LM_HEAD) {
+            quant_check();
+            m->Llm = make_qlayout(dtype, m->v_loc, H);
+            auto raw = slice_raw(data, dev, dtype, H, m->v0, m->v_loc, 0, H, s);
+            m->wlm = std::make_unique<DeviceBuffer>((size_t)m->Llm.total_bytes());
+            repack_into(m, m->Llm, m->wlm->ptr, raw->ptr, nibble_order, identity_map(m->Llm, 0, m->v_loc, 0), s);
+            m->global_set |= 4u;
+            return BEACON_CUDA_OK;
+        }
+        if (layer < 0 || layer >= c.num_layers) invalid("model_set_weight: bad layer");
+        LayerW& L = m->layers[layer];
+        switch (slot) {
+            case BEACON_CUDA_W_ATTN_NORM:
+                L.attn_norm = upload_plain_f32(data, dev, dtype, H, s);
+                L.set |= 1u << 0;
+                break;
+            case BEACON_CUDA_W_FFN_NORM:
+                L.ffn_norm = upload_plain_f32(data, dev, dtype, H, s);
+                L.set |= 1u << 1;
+                break;
+            case BEACON_CUDA_W_Q:
+            case BEACON_CUDA_W_K:
+            case BEACON_CUDA_W_V: {
+                quant_check();
+                m->Lqkv = make_qlayout(dtype, m->qkv_n, H);
+                if (!L.wqkv) {
+                    L.wqkv = std::make_unique<DeviceBuffer>((size_t)m->Lqkv.total_bytes());
+                    BC_CUDA(cudaMemset(L.wqkv->ptr, 0, (size_t)m->Lqkv.total_bytes()));
+                }
+                int64_t src0, nr, dst0;
+                if (slot == BEACON_CUDA_W_Q) {
+                    src0 = (int64_t)m->rank * m->h_loc * D; nr = m->qd; dst0 = 0;
+                } else {
+                    src0 = (int64_t)m->rank * m->kv_loc * D; nr = m->kd;
+                    dst0 = slot == BEACON_CUDA_W_K ? m->qd : m->qd + m->kd;
+                }
+                auto raw = slice_raw(data, dev, dtype, H, src0, nr, 0, H, s);
+                repack_into(m, m->Lqkv, L.wqkv->ptr, raw->ptr, nibble_order, identity_map(m->Lqkv, dst0, nr, 0), s);
+                L.set |= 1u << (2 + slot - BEACON_CUDA_W_Q);
+                break;
+            }
+            case BEACON_CUDA_W_O: {  // row-split: columns of this rank's heads
+                quant_check();
+                m->Lo = make_qlayout(dtype, H, m->qd);
+                auto raw = slice_raw(data, dev, dtype, (int64_t)c.num_heads * D, 0, H, (int64_t)m->rank * m->qd, m->qd, s);
+                L.wo = std::make_unique<DeviceBuffer>((size_t)m->Lo.total_bytes());
+                repack_into(m, m->Lo, L.wo->ptr, raw->ptr, nibble_order, identity_map(m->Lo, 0, H, 0), s);
+                L.set |= 1u << 5;
+                break;
+            }
+            case BEACON_CUDA_W_GATE:
+            case BEACON_CUDA_W_UP: {  // column-split, interleaved per 16 rows
+                quant_check();
+                const int64_t fl = m->f_loc;
+                if (fl % 16) shape_err("intermediate size per rank must be a multiple of 16");
+                m->Lgu = make_qlayout(dtype, 2 * fl, H);
+                if (!L.wgu) {
+                    L.wgu = std::make_unique<DeviceBuffer>((size_t)m->Lgu.total_bytes());
+                    BC_CUDA(cudaMemset(L.wgu->ptr, 0, (size_t)m->Lgu.total_bytes()));
+                }
+                auto raw = slice_raw(data, dev, dtype, H, (int64_t)m->rank * fl, fl, 0, H, s);
+                std::vector<int64_t> map((size_t)m->Lgu.n_pad, -2);
+                const bool up = slot == BEACON_CUDA_W_UP;
+                for (int64_t r = 0; r < m->Lgu.n_pad; ++r) {
+                    const int64_t lane = r % 32, f = (r / 32) * 16 + (lane % 16);
+                    if ((lane >= 16) == up) map[(size_t)r] = f < fl ? f : -1;
+                }
+                repack_into(m, m->Lgu, L.wgu->ptr, raw->ptr, nibble_order, map, s);
+                L.set |= 1u << (up ? 7 : 6);
+                break;
+            }
+            case BEACON_CUDA_W_DOWN: {  // row-split: columns of this rank's FFN slice
+                quant_check();
+                m->Ld = make_qlayout(dtype, H, m->f_loc);
+                auto raw = slice_raw(data, dev, dtype, c.intermediate_size, 0, H, (int64_t)m->rank * m->f_loc, m->f_loc, s);
+                L.wd = std::make_unique<DeviceBuffer>((size_t)m->Ld.total_bytes());
+                repack_into(m, m->Ld, L.wd->ptr, raw->ptr, nibble_order, identity_map(m->Ld, 0, H, 0), s);
+                L.set |= 1u << 8;
+                break;
+            }
+            default:
+                invalid("model_set_weight: unknown slot");
+        }
+        // (re)size the GEMV split-K scratch for every layout and batch in use
+        size_t need_p = 0;
+        int64_t need_c = 0;
+        for (const QLayout* Lp : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Ld, &m->Llm}) {
+            if (Lp->n == 0) continue;
+            for (int b = 1; b <= 16; ++b) {
+                GemvPlan pl = plan_qgemv(m->ctx, *Lp, b, gemv_mode(m));
+                if (pl.ksplit > 1) need_p = std::max(need_p, (size_t)pl.ksplit * b * Lp->n_pad);
+            }
+            need_c = std::max(need_c, Lp->groups());
+        }
+        if (need_p > m->gsc.partial_floats || need_c > m->gsc.counter_count) {
+            const size_t pf = std::max(need_p, m->gsc.partial_floats), cc = (size_t)std::max(need_c, m->gsc.counter_count);
+            const size_t coff = (pf * 4 + 255) / 256 * 256;
+            auto buf = std::make_unique<DeviceBuffer>(coff + cc * 4);
+            BC_CUDA(cudaMemset(buf->ptr, 0, coff + cc * 4));
+            m->gemv_buf = std::move(buf);
+            m->gsc.partial = static_cast<float*>(m->gemv_buf->ptr);
+            m->gsc.partial_floats = pf;
+            m->gsc.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(m->gemv_buf->ptr) + coff);
+            m->gsc.counter_count = (int64_t)cc;
+        }
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_reset(BeaconCudaModel* m) {
+    return guard([&]() -> int32_t {
+        require(m != nullptr, "model_reset: null argument");
+        set_device(m->ctx);
+        // Engine::reset_cache only rewinds current_length (engine.rs:176-180);
+        // the rows are overwritten before they are read again, but zeroing
+        // keeps the literal (non-persisting) mode exact.
+        const auto& c = m->cfg;
+        const size_t kvb = (size_t)c.max_batch * c.max_context * m->kd * (c.kv_dtype == BEACON_CUDA_DTYPE_F16 ? 2 : 4);
+        for (auto& L : m->layers) {
+            BC_CUDA(cudaMemset(L.kc->ptr, 0, kvb));
+            BC_CUDA(cudaMemset(L.vc->ptr, 0, kvb));
+        }
+        BC_CUDA(cudaDeviceSynchronize());
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_forward(BeaconCudaModel* m, BeaconCudaStream* stream, const uint32_t* tokens,
+                                  int32_t n_tokens, int32_t position, float* logits_out) {
+    return guard([&]() -> int32_t {
+        require(m && stream && tokens, "model_forward: null argument");
+        set_device(m->ctx);
+        check_ready(m);
+        const auto& c = m->cfg;
+        if (n_tokens <= 0) invalid("model_forward: empty token list");
+        if (position < 0) invalid("model_forward: negative position");
+        if ((int64_t)position + n_tokens > c.max_context) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
+        for (int i = 0; i < n_tokens; ++i)
+            if (tokens[i] >= (uint32_t)c.vocab_size) shape_err("embedding index out of bounds for the vocabulary");
+        if (!c.kv_persist && n_tokens > m->max_rows)
+            invalid("model_forward: the non-persisting cache mode needs the whole prompt in one chunk");
+        cudaStream_t s = stream->s;
+        if (!c.kv_persist) {
+            // cpu_backend.rs:459-460: the cache the engine holds is never
+            // written, so every call starts from zeros
+            const size_t kvb = (size_t)c.max_batch * c.max_context * m->kd * (c.kv_dtype == BEACON_CUDA_DTYPE_F16 ? 2 : 4);
+            for (auto& L : m->layers) {
+                BC_CUDA(cudaMemsetAsync(L.kc->ptr, 0, kvb, s));
+                BC_CUDA(cudaMemsetAsync(L.vc->ptr, 0, kvb, s));
+            }
+        }
+        const int64_t V = c.vocab_size;
+        for (int t0 = 0; t0 < n_tokens; t0 += m->max_rows) {
+            const int rows = std::min(m->max_rows, n_tokens - t0);
+            for (int i = 0; i < rows; ++i) m->h_stage[i] = (int32_t)tokens[t0 + i];
+            BC_CUDA(cudaMemcpyAsync(m->tok, m->h_stage, (size_t)rows * 4, cudaMemcpyHostToDevice, s));
+            embed_kernel<<<rows, 256, 0, s>>>(m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, V, c.hidden_size,
+                                              m->tok, m->h, m->err_dev);
+            BC_LAUNCHED("embed_kernel");
+            run_layers(m, rows, false, nullptr, position + t0, s);
+            finish_logits(m, rows, true, false, s);
+            if (logits_out)
+                BC_CUDA(cudaMemcpyAsync(logits_out + (int64_t)t0 * V, full_logits(m), (size_t)rows * V * 4,
+                                        cudaMemcpyDeviceToHost, s));
+            BC_CUDA(cudaStreamSynchronize(s));
+        }
+        check_err(m, s);
+        return BEACON_CUDA_OK;
+    });
+}
+
+static void launch_decode_graph(BeaconCudaModel* m, int batch, bool autoregressive, cudaStream_t s) {
+    const int key = batch * 2 + (autoregressive ? 1 : 0);
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        // One eager run first, so kernel modules load outside the capture. The
+        // host-fed body only rewrites the same cache rows from the same inputs.
+        decode_body(m, batch, false, s);
+        BC_CUDA(cudaStreamSynchronize(s));
+        cudaGraph_t g = nullptr;
+        BC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        try {
+            decode_body(m, batch, autoregressive, s);
+        } catch (...) {
+            cudaStreamEndCapture(s, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        BC_CUDA(cudaStreamEndCapture(s, &g));
+        cudaGraphExec_t ge = nullptr;
+        cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        cuda_check(e, "cudaGraphInstantiate");
+        it = m->graphs.emplace(key, ge).first;
+    }
+    BC_CUDA(cudaGraphLaunch(it->second, s));
+}
+
+int32_t beacon_cuda_model_decode_step(BeaconCudaModel* m, BeaconCudaStream* stream, const uint32_t* tokens,
+                                      int32_t batch, int32_t position, uint32_t* next_tokens, float* logits_out) {
+    return guard([&]() -> int32_t {
+        require(m && stream && tokens, "model_decode_step: null argument");
+        set_device(m->ctx);
+        check_ready(m);
+        const auto& c = m->cfg;
+        if (batch <= 0 || batch > c.max_batch) invalid("model_decode_step: batch out of range");
+        if (position < 0 || position + 1 > c.max_context) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
+        for (int i = 0; i < batch; ++i)
+            if (tokens[i] >= (uint32_t)c.vocab_size) shape_err("embedding index out of bounds for the vocabulary");
+        cudaStream_t s = stream->s;
+        m->h_stage[0] = position;
+        for (int i = 0; i < batch; ++i) m->h_stage[1 + i] = (int32_t)tokens[i];
+        BC_CUDA(cudaMemcpyAsync(m->pos_dev, m->h_stage, 4, cudaMemcpyHostToDevice, s));
+        BC_CUDA(cudaMemcpyAsync(m->tok, m->h_stage + 1, (size_t)batch * 4, cudaMemcpyHostToDevice, s));
+        if (!c.kv_persist) {
+            const size_t kvb = (size_t)c.max_batch * c.max_context * m->kd * (c.kv_dtype == BEACON_CUDA_DTYPE_F16 ? 2 : 4);
+            for (auto& L : m->layers) {
+                BC_CUDA(cudaMemsetAsync(L.kc->ptr, 0, kvb, s));
+                BC_CUDA(cudaMemsetAsync(L.vc->ptr, 0, kvb, s));
+            }
+        }
+        launch_decode_graph(m, batch, false, s);
+        if (next_tokens) BC_CUDA(cudaMemcpyAsync(m->h_next, m->next, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
+        if (logits_out)
+            BC_CUDA(cudaMemcpyAsync(logits_out, full_logits(m), (size_t)batch * c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
+        BC_CUDA(cudaStreamSynchronize(s));
+        if (next_tokens)
+            for (int i = 0; i < batch; ++i) next_tokens[i] = (uint32_t)m->h_next[i];
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_decode_step_device(BeaconCudaModel* m, BeaconCudaStream* stream, const int32_t* d_tokens,
+                                             int32_t batch, int32_t position, int32_t* d_next_tokens,
+                                             float* d_logits) {
+    return guard([&]() -> int32_t {
+        require(m && stream, "model_decode_step_device: null argument");
+        set_device(m->ctx);
+        check_ready(m);
+        const auto& c = m->cfg;
+        if (batch <= 0 || batch > c.max_batch) invalid("model_decode_step_device: batch out of range");
+        cudaStream_t s = stream->s;
+        // d_tokens == NULL and position < 0: continue from the previous step on
+        // the device (tokens = last argmax, position advanced in the graph).
+        const bool autoregressive = d_tokens == nullptr && position < 0;
+        if (!autoregressive) {
+            require(d_tokens != nullptr, "model_decode_step_device: tokens required unless continuing");
+            if (position + 1 > c.max_context) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
+            m->h_stage[0] = position;
+            BC_CUDA(cudaMemcpyAsync(m->pos_dev, m->h_stage, 4, cudaMemcpyHostToDevice, s));
+            if (d_tokens != m->tok)
+                BC_CUDA(cudaMemcpyAsync(m->tok, d_tokens, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+        }
+        launch_decode_graph(m, batch, autoregressive, s);
+        if (d_next_tokens) BC_CUDA(cudaMemcpyAsync(d_next_tokens, m->next, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+        if (d_logits)
+            BC_CUDA(cudaMemcpyAsync(d_logits, full_logits(m), (size_t)batch * c.vocab_size * 4, cudaMemcpyDeviceToDevice, s));
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* m, BeaconCudaStream* stream, int32_t slot, int32_t batch,
+                                         int32_t iters, float* out_avg_us, uint64_t* out_bytes) {
+    return guard([&]() -> int32_t {
+        require(m && stream && out_avg_us && out_bytes, "model_profile_linear: null argument");
+        set_device(m->ctx);
+        check_ready(m);
+        if (batch < 1 || batch > std::min(16, m->max_rows) || iters < 1) invalid("model_profile_linear: bad batch/iters");
+        cudaStream_t s = stream->s;
+        const int64_t hid = m->cfg.hidden_size;
+        const QLayout* Lp;
+        const float* x;
+        int64_t x_ld, y_ld, out_n;
+        float* y;
+        int epi = EPI_STORE;
+        switch (slot) {
+            case BEACON_CUDA_W_Q: Lp = &m->Lqkv; x = m->xn; x_ld = hid; y = m->qkv; y_ld = m->qkv_n; out_n = m->qkv_n; break;
+            case BEACON_CUDA_W_O: Lp = &m->Lo; x = m->attn; x_ld = m->qd; y = m->xn; y_ld = hid; out_n = hid; break;
+            case BEACON_CUDA_W_GATE: Lp = &m->Lgu; x = m->xn; x_ld = hid; y = m->ffn; y_ld = m->f_loc; out_n = m->f_loc;
+                epi = EPI_SWIGLU; break;
+            case BEACON_CUDA_W_DOWN: Lp = &m->Ld; x = m->ffn; x_ld = m->f_loc; y = m->xn; y_ld = hid; out_n = hid; break;
+            case BEACON_CUDA_W_LM_HEAD: Lp = &m->Llm; x = m->xn; x_ld = hid; y = m->logits_loc; y_ld = m->v_loc;
+                out_n = m->v_loc; break;
+            default: invalid("model_profile_linear: slot must be Q, O, GATE, DOWN or LM_HEAD");
+        }
+        const int nl = slot == BEACON_CUDA_W_LM_HEAD ? 1 : m->cfg.num_layers;
+        auto weight = [&](int li) -> const void* {
+            const LayerW& L = m->layers[li];
+            switch (slot) {
+                case BEACON_CUDA_W_Q: return L.wqkv->ptr;
+                case BEACON_CUDA_W_O: return L.wo->ptr;
+                case BEACON_CUDA_W_GATE: return L.wgu->ptr;
+                case BEACON_CUDA_W_DOWN: return L.wd->ptr;
+                default: return m->wlm->ptr;
+            }
+        };
+        auto pass = [&]() {
+            for (int li = 0; li < nl; ++li)
+                linear(m, *Lp, weight(li), x, x_ld, batch, y, y_ld, epi, nullptr, 0, s);
+        };
+        pass();  // warm-up
+        cudaEvent_t e0, e1;
+        BC_CUDA(cudaEventCreate(&e0));
+        BC_CUDA(cudaEventCreate(&e1));
+        BC_CUDA(cudaEventRecord(e0, s));
+        for (int it = 0; it < iters; ++it) pass();
+        BC_CUDA(cudaEventRecord(e1, s));
+        BC_CUDA(cudaEventSynchronize(e1));
+        float ms = 0.0f;
+        BC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *out_avg_us = ms * 1000.0f / (float)(iters * nl);
+        const int64_t wbytes = Lp->n * (Lp->k / block_size(Lp->dtype)) * block_bytes(Lp->dtype);
+        *out_bytes = (uint64_t)(wbytes + (int64_t)batch * Lp->k * 4 + (int64_t)batch * out_n * 4);
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_memory(const BeaconCudaModel* m, uint64_t* out_bytes) {
+    return guard([&]() -> int32_t {
+        require(m && out_bytes, "model_memory: null argument");
+        uint64_t t = 0;
+        auto add = [&](const std::unique_ptr<DeviceBuffer>& b) {
+            if (b) t += b->bytes;
+        };
+        for (const auto& L : m->layers) {
+            add(L.attn_norm); add(L.ffn_norm); add(L.wqkv); add(L.wo); add(L.wgu); add(L.wd); add(L.kc); add(L.vc);
+        }
+        add(m->embed); add(m->final_norm); add(m->wlm); add(m->rope_cs); add(m->rope_sn); add(m->act);
+        add(m->gemv_buf); add(m->attn_buf);
+        *out_bytes = t;
+        return BEACON_CUDA_OK;
+    });
+}
+
+}  // extern "C"

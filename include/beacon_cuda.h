@@ -1,0 +1,298 @@
+/*
+ * beacon_cuda.h -- C ABI of the B200 (sm_100a) backend for Beacon's
+ * quantized decode path.
+ *
+ * This is the surface a `beacon-cuda` crate binds to implement beacon-core's
+ * `ComputeBackend` trait (crates/beacon-core/src/backend.rs:14-167). It copies
+ * the conventions of the MLX shim (shim/include/beacon_shim.h):
+ *   - opaque handles (beacon_shim.h:18-21);
+ *   - every call returns an int32_t status, BEACON_CUDA_OK == 0
+ *     (beacon_shim.h:24-33), output parameters come last;
+ *   - *_destroy returns void;
+ *   - beacon_cuda_last_error_message() is thread-local and valid until the
+ *     next call on the same thread (beacon_shim.h:222-227,
+ *     shim/src/errors.cpp:13);
+ *   - C++ exceptions never cross the ABI (shim/src/guard.h:12-39): bad_alloc
+ *     maps to OUT_OF_MEMORY, invalid_argument to INVALID_ARGUMENT,
+ *     out_of_range to SHAPE_MISMATCH.
+ * No torch or CUDA types appear in any signature: streams and device
+ * pointers travel as void*.
+ *
+ * Quantized weights are uploaded as raw GGUF block bytes, row-major [N, K]
+ * with blocks along K (crates/beacon-format/src/gguf/tensor_info.rs:40-48).
+ * The tensor remembers its block type, so `quantized_matmul` needs no
+ * separate scales/biases tensors (they are MLX-affine only and may be NULL).
+ */
+#ifndef BEACON_CUDA_H
+#define BEACON_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* === Handles (opaque) === */
+typedef struct BeaconCudaContext BeaconCudaContext;
+typedef struct BeaconCudaStream BeaconCudaStream;
+typedef struct BeaconCudaTensor BeaconCudaTensor;
+typedef struct BeaconCudaModel BeaconCudaModel;
+
+/* === Status codes (values 0-4 and 99 as BeaconStatus, beacon_shim.h:24-33) === */
+typedef enum {
+    BEACON_CUDA_OK = 0,
+    BEACON_CUDA_ERR_INVALID_ARGUMENT = 1,
+    BEACON_CUDA_ERR_OUT_OF_MEMORY = 2,
+    BEACON_CUDA_ERR_SHAPE_MISMATCH = 3,
+    BEACON_CUDA_ERR_UNSUPPORTED_DTYPE = 4,
+    BEACON_CUDA_ERR_KERNEL_LAUNCH = 5,  /* slot of BEACON_ERR_METAL_COMPILE */
+    BEACON_CUDA_ERR_CUDA = 6,           /* slot of BEACON_ERR_MLX_INTERNAL */
+    BEACON_CUDA_ERR_CONTEXT_OVERFLOW = 7, /* EngineError::ContextOverflow (error.rs:24-26) */
+    BEACON_CUDA_ERR_COMM = 8,           /* NCCL failure or timeout */
+    BEACON_CUDA_ERR_DEVICE_TIMEOUT = 9, /* a bounded device-side wait ran out */
+    BEACON_CUDA_ERR_UNKNOWN = 99
+} BeaconCudaStatus;
+
+/* === Dtypes: the BeaconDtype discriminants (crates/beacon-format/src/dtype.rs:12-29) === */
+typedef enum {
+    BEACON_CUDA_DTYPE_F32 = 0,
+    BEACON_CUDA_DTYPE_F16 = 1,
+    BEACON_CUDA_DTYPE_BF16 = 2,
+    BEACON_CUDA_DTYPE_I32 = 3,
+    BEACON_CUDA_DTYPE_I8 = 4,
+    BEACON_CUDA_DTYPE_Q4_0 = 100,
+    BEACON_CUDA_DTYPE_Q4_K = 101,
+    BEACON_CUDA_DTYPE_Q5_K = 102,
+    BEACON_CUDA_DTYPE_Q6_K = 103,
+    BEACON_CUDA_DTYPE_Q8_0 = 104,
+    BEACON_CUDA_DTYPE_Q4_1 = 105,
+    BEACON_CUDA_DTYPE_Q5_0 = 106,
+    BEACON_CUDA_DTYPE_Q5_1 = 107,
+    BEACON_CUDA_DTYPE_Q2_K = 108,
+    BEACON_CUDA_DTYPE_Q3_K = 109,
+    BEACON_CUDA_DTYPE_Q8_K = 110
+} BeaconCudaDtype;
+
+/* Q4_0 nibble order of uploaded bytes. REF_INTERLEAVED is what the reference's
+ * CPU code computes (byte i -> elements 2i, 2i+1; dequant.rs:170-176,
+ * q4.rs:33-41). GGUF_SPLIT is the GGUF file order (byte i -> i, i+16). */
+typedef enum {
+    BEACON_CUDA_NIBBLE_REF_INTERLEAVED = 0,
+    BEACON_CUDA_NIBBLE_GGUF_SPLIT = 1
+} BeaconCudaNibbleOrder;
+
+/* Arithmetic of quantized_matmul and of the model's linears.
+ *  FAST:    activations quantized per 32 elements to int16, integer dot
+ *           products (dp2a) against the 4/8-bit codes, f32 block scaling.
+ *  EXACT:   f32 activations times the unrounded f32 weight q*d (the values
+ *           of q4::dequantize_q4_0_block, q4.rs:26-42), f32 accumulation.
+ *  REF_RTZ: f32 activations times the f16-truncated weights that the CPU
+ *           engine consumes (f16_to_f32(dequantize_to_f16(.)),
+ *           dequant.rs:33-60), f32 accumulation. */
+typedef enum {
+    BEACON_CUDA_NUMERICS_FAST = 0,
+    BEACON_CUDA_NUMERICS_EXACT = 1,
+    BEACON_CUDA_NUMERICS_REF_RTZ = 2
+} BeaconCudaNumerics;
+
+/* === Lifecycle (beacon_shim.h:49-54) === */
+int32_t beacon_cuda_context_create(int32_t device, BeaconCudaContext** out_ctx);
+void    beacon_cuda_context_destroy(BeaconCudaContext* ctx);
+int32_t beacon_cuda_context_set_numerics(BeaconCudaContext* ctx, int32_t numerics);
+
+int32_t beacon_cuda_stream_create(BeaconCudaContext* ctx, BeaconCudaStream** out_stream);
+/* Borrow an existing cudaStream_t (passed as void*); destroy does not free it. */
+int32_t beacon_cuda_stream_wrap(BeaconCudaContext* ctx, void* cuda_stream,
+                                BeaconCudaStream** out_stream);
+void    beacon_cuda_stream_destroy(BeaconCudaStream* stream);
+int32_t beacon_cuda_stream_synchronize(BeaconCudaStream* stream);
+
+/* === Tensors (beacon_shim.h:56-88) === */
+/* Replaces beacon_tensor_from_mmap (beacon_shim.h:59-64): copies host bytes
+ * to the device once. Quantized: shape is the logical [N, K] element shape and
+ * `host` holds N * K / block_size GGUF blocks. */
+int32_t beacon_cuda_tensor_upload(BeaconCudaContext* ctx, const void* host,
+                                  const int64_t* shape, size_t ndim, int32_t dtype,
+                                  int32_t nibble_order, BeaconCudaTensor** out_tensor);
+/* Same as upload but the GGUF bytes are already in device memory. */
+int32_t beacon_cuda_tensor_from_device_blocks(BeaconCudaContext* ctx, const void* device_bytes,
+                                              const int64_t* shape, size_t ndim, int32_t dtype,
+                                              int32_t nibble_order, BeaconCudaTensor** out_tensor);
+/* beacon_tensor_zeros (beacon_shim.h:66-71). */
+int32_t beacon_cuda_tensor_zeros(BeaconCudaContext* ctx, const int64_t* shape, size_t ndim,
+                                 int32_t dtype, BeaconCudaTensor** out_tensor);
+/* Non-owning view of caller device memory (plain dtypes only). */
+int32_t beacon_cuda_tensor_wrap_device(BeaconCudaContext* ctx, void* device_ptr,
+                                       const int64_t* shape, size_t ndim, int32_t dtype,
+                                       BeaconCudaTensor** out_tensor);
+void    beacon_cuda_tensor_destroy(BeaconCudaTensor* tensor);
+int32_t beacon_cuda_tensor_shape(const BeaconCudaTensor* t, int64_t* out_shape, size_t* inout_ndim);
+int32_t beacon_cuda_tensor_dtype(const BeaconCudaTensor* t, int32_t* out_dtype);
+int32_t beacon_cuda_tensor_device_ptr(const BeaconCudaTensor* t, void** out_ptr);
+/* beacon_tensor_eval (beacon_shim.h:84): waits for the stream. */
+int32_t beacon_cuda_tensor_eval(BeaconCudaTensor* t, BeaconCudaStream* stream);
+/* beacon_tensor_read_f32 (beacon_shim.h:88); F16/BF16/I32 are converted. */
+int32_t beacon_cuda_tensor_read_f32(const BeaconCudaTensor* t, float* out, size_t n_elements);
+int32_t beacon_cuda_tensor_read_raw(const BeaconCudaTensor* t, void* out, size_t n_bytes);
+
+/* === Ops: ComputeBackend methods (backend.rs:21-166; beacon_shim.h:90-189) === */
+int32_t beacon_cuda_op_matmul(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                              const BeaconCudaTensor* a, const BeaconCudaTensor* b,
+                              BeaconCudaTensor** out);
+/* backend.rs:32-41: out = x @ dequant(w)^T, x [S, K] (F32 or F16), out [S, N] F32.
+ * scales/biases may be NULL; group_size/bits must agree with w's block type
+ * (32/4 Q4_0, 32/8 Q8_0, 256/4 Q4_K) or be 0. */
+int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                        const BeaconCudaTensor* x, const BeaconCudaTensor* w,
+                                        const BeaconCudaTensor* scales,
+                                        const BeaconCudaTensor* biases, int32_t group_size,
+                                        int32_t bits, BeaconCudaTensor** out);
+int32_t beacon_cuda_op_rms_norm(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                const BeaconCudaTensor* x, const BeaconCudaTensor* weight,
+                                float eps, BeaconCudaTensor** out);
+/* Interleaved-pair RoPE of the CPU backend (ops.rs:124-142, cpu_backend.rs:141-180);
+ * freqs (custom frequencies) may be NULL. */
+int32_t beacon_cuda_op_rope(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                            const BeaconCudaTensor* x, int32_t position_offset, float theta,
+                            int32_t dim, const BeaconCudaTensor* freqs, BeaconCudaTensor** out);
+int32_t beacon_cuda_op_silu(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                            const BeaconCudaTensor* x, BeaconCudaTensor** out);
+int32_t beacon_cuda_op_softmax(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                               const BeaconCudaTensor* x, int32_t axis, BeaconCudaTensor** out);
+/* q [B, H, Sq, D], k/v [B, Hkv, Skv, D]; mask (additive, NULL = none).
+ * `causal`: -1 = as the MLX shim (causal when mask is NULL and Sq > 1,
+ * shim/src/ops.cpp:216-223), 0 = never (cpu_backend.rs:511-598), 1 = always. */
+int32_t beacon_cuda_op_attention(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                 const BeaconCudaTensor* q, const BeaconCudaTensor* k,
+                                 const BeaconCudaTensor* v, const BeaconCudaTensor* mask,
+                                 float scale, int32_t causal, BeaconCudaTensor** out);
+int32_t beacon_cuda_op_add(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                           const BeaconCudaTensor* a, const BeaconCudaTensor* b,
+                           BeaconCudaTensor** out);
+int32_t beacon_cuda_op_elementwise_mul(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                       const BeaconCudaTensor* a, const BeaconCudaTensor* b,
+                                       BeaconCudaTensor** out);
+/* backend.rs:152-160 / beacon_shim.h:155-160. Writes new_k/new_v [S, Hkv, D]
+ * into the caches [max_ctx, Hkv, D] at `position` IN PLACE (the MLX
+ * semantics, shim/src/ops.cpp:318-324) and returns views of rows
+ * [0, position + S). */
+int32_t beacon_cuda_op_kv_cache_update(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                       BeaconCudaTensor* cache_k, BeaconCudaTensor* cache_v,
+                                       const BeaconCudaTensor* new_k,
+                                       const BeaconCudaTensor* new_v, int64_t position,
+                                       BeaconCudaTensor** out_k_view,
+                                       BeaconCudaTensor** out_v_view);
+int32_t beacon_cuda_op_reshape(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                               const BeaconCudaTensor* x, const int64_t* new_shape,
+                               size_t new_ndim, BeaconCudaTensor** out);
+int32_t beacon_cuda_op_transpose(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                 const BeaconCudaTensor* x, BeaconCudaTensor** out);
+int32_t beacon_cuda_op_swapaxes(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                const BeaconCudaTensor* x, int32_t axis1, int32_t axis2,
+                                BeaconCudaTensor** out);
+/* weight [vocab, hidden] (F16/F32), indices I32 or F32 (cpu_backend.rs:387-418). */
+int32_t beacon_cuda_op_embedding(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                 const BeaconCudaTensor* weight, const BeaconCudaTensor* indices,
+                                 BeaconCudaTensor** out);
+/* backend.rs:166: token ids -> I32 tensor [n]. */
+int32_t beacon_cuda_create_token_tensor(BeaconCudaContext* ctx, const uint32_t* tokens,
+                                        size_t n, BeaconCudaTensor** out);
+/* Greedy argmax per row of the last dim with the reference's rule: last index
+ * among equal maxima, NaN compares equal (sampling.rs:60-66). out: I32 [rows]. */
+int32_t beacon_cuda_op_argmax(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                              const BeaconCudaTensor* logits, BeaconCudaTensor** out);
+/* dequantize_to_f16 (dequant.rs:33-60), bit-exact: out F16 [N, K]. */
+int32_t beacon_cuda_op_dequantize_to_f16(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                         const BeaconCudaTensor* w, BeaconCudaTensor** out);
+/* f32 [N, K] -> GGUF blocks (Q4_0, Q8_0, Q4_K), returned as a quantized tensor.
+ * The same deterministic quantizer as the test fixtures; no reference
+ * counterpart (the reference has no GGUF quantizer). */
+int32_t beacon_cuda_op_quantize(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                const BeaconCudaTensor* x, int32_t dtype, int32_t nibble_order,
+                                BeaconCudaTensor** out);
+
+/* Device-to-device form of the quantizer: d_x f32 [n_rows, k] -> GGUF block
+ * bytes at d_out (n_rows * k / block_size * block_bytes bytes), enqueued on
+ * `stream`. No reference counterpart (fixture/synthetic-weight generation). */
+int32_t beacon_cuda_quantize_blocks(BeaconCudaContext* ctx, BeaconCudaStream* stream, const float* d_x,
+                                    int64_t n_rows, int64_t k, int32_t dtype, int32_t nibble_order,
+                                    void* d_out);
+
+/* === Fused decoder runtime (Engine<B>::forward, engine.rs:190-456) === */
+typedef struct {
+    int32_t vocab_size, hidden_size, num_layers, num_heads, num_kv_heads, head_dim;
+    int32_t intermediate_size, max_context, max_batch;
+    float rope_theta, rms_norm_eps;
+    int32_t numerics;      /* BeaconCudaNumerics */
+    int32_t kv_dtype;      /* BEACON_CUDA_DTYPE_F16 or _F32 */
+    int32_t kv_persist;    /* 0 reproduces cpu_backend.rs:459-460 (cache never written back) */
+    int32_t causal_prefill;/* 0 reproduces engine.rs:418 (mask None) */
+    int32_t tp_size, tp_rank;
+} BeaconCudaModelConfig;
+
+/* Weight slots (also used by the oracle). */
+typedef enum {
+    BEACON_CUDA_W_EMBED = 0, BEACON_CUDA_W_FINAL_NORM = 1, BEACON_CUDA_W_LM_HEAD = 2,
+    BEACON_CUDA_W_ATTN_NORM = 10, BEACON_CUDA_W_Q = 11, BEACON_CUDA_W_K = 12,
+    BEACON_CUDA_W_V = 13, BEACON_CUDA_W_O = 14, BEACON_CUDA_W_FFN_NORM = 15,
+    BEACON_CUDA_W_GATE = 16, BEACON_CUDA_W_UP = 17, BEACON_CUDA_W_DOWN = 18
+} BeaconCudaWeightSlot;
+
+int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelConfig* cfg,
+                                 BeaconCudaModel** out_model);
+void    beacon_cuda_model_destroy(BeaconCudaModel* model);
+/* Full (unsharded) tensor bytes: GGUF blocks for linears, F16/F32 for norms
+ * and embeddings. `on_device` != 0: `data` is a device pointer. Under tensor
+ * parallelism each rank keeps only its shard. */
+int32_t beacon_cuda_model_set_weight(BeaconCudaModel* model, int32_t layer, int32_t slot,
+                                     const void* data, int32_t dtype, int32_t nibble_order,
+                                     int32_t on_device);
+/* Engine::reset_cache (engine.rs:176-180). */
+int32_t beacon_cuda_model_reset(BeaconCudaModel* model);
+/* Engine::forward (engine.rs:190-241) for one sequence: tokens (host) ->
+ * logits [n_tokens, vocab] F32 written to host `logits_out` (NULL: skip). */
+int32_t beacon_cuda_model_forward(BeaconCudaModel* model, BeaconCudaStream* stream,
+                                  const uint32_t* tokens, int32_t n_tokens, int32_t position,
+                                  float* logits_out);
+/* One greedy decode step for `batch` independent sequences at the same
+ * position: tokens [batch] (host) -> next tokens [batch] (host), and logits
+ * [batch, vocab] to host when logits_out != NULL. Engine::generate_next_token
+ * (engine.rs:249-264) for batch == 1. */
+int32_t beacon_cuda_model_decode_step(BeaconCudaModel* model, BeaconCudaStream* stream,
+                                      const uint32_t* tokens, int32_t batch, int32_t position,
+                                      uint32_t* next_tokens, float* logits_out);
+/* Same step with device buffers (int32 tokens in, int32 next tokens out,
+ * logits F32 [batch, vocab] or NULL); enqueued only, nothing is copied. */
+int32_t beacon_cuda_model_decode_step_device(BeaconCudaModel* model, BeaconCudaStream* stream,
+                                             const int32_t* d_tokens, int32_t batch,
+                                             int32_t position, int32_t* d_next_tokens,
+                                             float* d_logits);
+/* Times `iters` passes of one projection over every layer, using the decode
+ * step's own kernels and buffers (each layer's weight is distinct, so reads
+ * are L2-cold), with CUDA events on `stream`. slot: BEACON_CUDA_W_Q (the fused
+ * q/k/v GEMV), _O, _GATE (the fused gate/up GEMV with SwiGLU), _DOWN or
+ * _LM_HEAD. out_avg_us: mean duration of one launch; out_bytes: algorithmic
+ * bytes of one launch (weight blocks + f32 activations in + f32 out). */
+int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* model, BeaconCudaStream* stream, int32_t slot,
+                                         int32_t batch, int32_t iters, float* out_avg_us,
+                                         uint64_t* out_bytes);
+/* Bytes of device memory held by the model (weights + KV cache + workspace). */
+int32_t beacon_cuda_model_memory(const BeaconCudaModel* model, uint64_t* out_bytes);
+
+/* === Tensor parallelism (NCCL over NVLink) === */
+/* 128-byte ncclUniqueId, made on rank 0 and shared by the caller. */
+int32_t beacon_cuda_comm_unique_id(void* out_id_128);
+int32_t beacon_cuda_comm_init(BeaconCudaContext* ctx, int32_t nranks, int32_t rank,
+                              const void* id_128, int32_t timeout_ms);
+int32_t beacon_cuda_op_all_reduce_f32(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                      BeaconCudaTensor* t);
+
+/* === Error introspection (beacon_shim.h:222-227) === */
+const char* beacon_cuda_last_error_message(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BEACON_CUDA_H */
