@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a
         qs[g][dd] = a.q[((int64_t)b * a.heads + kvh * G + g) * D + dd] * a.scale;
     }
     __syncthreads();
-    const int kv_len = a.pos_ptr ? *a.pos_ptr + 1 : a.kv_len;
+    const int kv_len = max(1, min(a.max_kv, a.pos_ptr ? *a.pos_ptr + 1 : a.kv_len));
     const int chunk = ((kv_len + a.nsplit - 1) / a.nsplit + 31) / 32 * 32;
     const int64_t k0 = (int64_t)split * chunk;
     const int64_t k1 = min((int64_t)kv_len, k0 + chunk);

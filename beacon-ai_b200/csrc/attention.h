@@ -40,6 +40,7 @@ struct DecodeAttnArgs {
     int batch, heads, kv_heads, d;
     int kv_len;        // keys [0, kv_len) are attended ...
     const int* pos_ptr;  // ... or, when set, keys [0, *pos_ptr + 1) (graph replay)
+    int max_kv;          // cache rows; kv_len is clamped to it
     float scale;
     int nsplit;
     float* part_acc;

@@ -87,10 +87,14 @@ __global__ void rope_table_kernel(float* cs, float* sn, int max_ctx, int d, floa
 template <typename KV>
 __global__ void qkv_post_kernel(const float* qkv, float* q, KV* kc, KV* vc, const float* cs, const float* sn,
                                 int rows, int qd, int kd, int d, int64_t cache_sb, const int* pos_ptr, int pos_imm,
-                                int pos_step, int seq_step) {
+                                int pos_step, int seq_step, int max_ctx, int* err) {
     const int r = blockIdx.y;
     const int pos0 = read_pos(pos_ptr, pos_imm);
     const int pos = pos0 + r * pos_step;
+    if (pos < 0 || pos >= max_ctx) {  // a device-advanced position ran past the cache
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 2);
+        return;
+    }
     const int seq = r * seq_step;
     const int qkvn = qd + 2 * kd;
     const float* src = qkv + (int64_t)r * qkvn;
@@ -279,12 +283,14 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
                 qkv_post_kernel<__half><<<grid, 256, 0, s>>>(
                     m->qkv, m->q, static_cast<__half*>(L.kc->ptr), static_cast<__half*>(L.vc->ptr),
                     static_cast<const float*>(m->rope_cs->ptr), static_cast<const float*>(m->rope_sn->ptr), rows,
-                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step);
+                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step, c.max_context,
+                    m->err_dev);
             else
                 qkv_post_kernel<float><<<grid, 256, 0, s>>>(
                     m->qkv, m->q, static_cast<float*>(L.kc->ptr), static_cast<float*>(L.vc->ptr),
                     static_cast<const float*>(m->rope_cs->ptr), static_cast<const float*>(m->rope_sn->ptr), rows,
-                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step);
+                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step, c.max_context,
+                    m->err_dev);
             BC_LAUNCHED("qkv_post_kernel");
         }
         const float scale = 1.0f / sqrtf((float)D);  // engine.rs:415
@@ -301,6 +307,7 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.d = D;
             a.pos_ptr = pos_ptr;
             a.kv_len = pos_imm + 1;
+            a.max_kv = c.max_context;
             a.scale = scale;
             a.nsplit = m->attn_nsplit;
             a.part_acc = m->pacc;
@@ -395,6 +402,7 @@ void check_err(BeaconCudaModel* m, cudaStream_t s) {
     BC_CUDA(cudaStreamSynchronize(s));
     if (herr) {
         BC_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), s));
+        if (herr == 2) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
         shape_err("token id out of range for the vocabulary");
     }
 }
