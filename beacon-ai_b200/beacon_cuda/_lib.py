@@ -107,6 +107,9 @@ SIGNATURES = {
     "beacon_cuda_model_decode_step_device": (_I32, [_P, _P, _P, _I32, _I32, _P, _P]),
     "beacon_cuda_model_profile_linear": (_I32, [_P, _P, _I32, _I32, _I32, ctypes.POINTER(ctypes.c_float),
                                                 ctypes.POINTER(ctypes.c_uint64)]),
+    "beacon_cuda_model_fill_kv_random": (_I32, [_P, _I32, ctypes.c_uint64]),
+    "beacon_cuda_model_launches_per_step": (_I32, [_P, _I32, _I32, ctypes.POINTER(_I32)]),
+    "beacon_cuda_stream_handle": (_I32, [_P, _PP]),
     "beacon_cuda_model_memory": (_I32, [_P, ctypes.POINTER(ctypes.c_uint64)]),
     "beacon_cuda_comm_unique_id": (_I32, [_P]),
     "beacon_cuda_comm_init": (_I32, [_P, _I32, _I32, _P, _I32]),

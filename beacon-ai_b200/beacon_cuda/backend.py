@@ -123,6 +123,13 @@ class Stream:
     def synchronize(self) -> None:
         _raise(L.lib().beacon_cuda_stream_synchronize(self._h))
 
+    @property
+    def cuda_stream(self) -> int:
+        """The underlying cudaStream_t, e.g. for torch.cuda.ExternalStream."""
+        p = ctypes.c_void_p()
+        _raise(L.lib().beacon_cuda_stream_handle(self._h, ctypes.byref(p)))
+        return p.value or 0
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:

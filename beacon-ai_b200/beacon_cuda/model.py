@@ -101,6 +101,14 @@ class CudaModel:
                                                         ctypes.byref(us), ctypes.byref(nb)))
         return us.value, nb.value
 
+    def fill_kv_random(self, n_rows: int, seed: int = 0) -> None:
+        _raise(L.lib().beacon_cuda_model_fill_kv_random(self._h, n_rows, seed))
+
+    def launches_per_step(self, batch: int, continuing: bool) -> int:
+        v = ctypes.c_int32()
+        _raise(L.lib().beacon_cuda_model_launches_per_step(self._h, batch, int(continuing), ctypes.byref(v)))
+        return v.value
+
     def memory_bytes(self) -> int:
         v = ctypes.c_uint64()
         _raise(L.lib().beacon_cuda_model_memory(self._h, ctypes.byref(v)))

@@ -46,6 +46,19 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
     }
 }
 
+GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const GemvPlan& pl, int batch, const QLayout& L,
+                                 cudaStream_t s) {
+    GemvScratch sc;
+    if (pl.ksplit <= 1) return sc;
+    if ((size_t)L.groups() > Workspace::kCounterInts) shape_err("too many rows for the split-K counters");
+    const size_t pf = (size_t)pl.ksplit * batch * L.n_pad;
+    sc.partial = static_cast<float*>(ctx->ws.get(pf * sizeof(float), s));
+    sc.partial_floats = pf;
+    sc.counters = ctx->ws.counters();
+    sc.counter_count = (int64_t)Workspace::kCounterInts;
+    return sc;
+}
+
 // Prefill-sized matmul through the GEMV in 16-row chunks (each chunk streams
 // the weight once). Numerics follow the context's mode exactly.
 void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTensor* w, const void* x, bool x_f16,
@@ -57,16 +70,7 @@ void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTenso
     for (int64_t r0 = 0; r0 < rows; r0 += 16) {
         const int b = (int)std::min<int64_t>(16, rows - r0);
         GemvPlan pl = plan_qgemv(ctx, L, b, mode);
-        GemvScratch sc;
-        if (pl.ksplit > 1) {
-            size_t pf = (size_t)pl.ksplit * b * L.n_pad;
-            size_t coff = (pf * 4 + 255) / 256 * 256;
-            uint8_t* base = static_cast<uint8_t*>(ctx->ws.get(coff + (size_t)L.groups() * 4, s));
-            sc.partial = reinterpret_cast<float*>(base);
-            sc.partial_floats = pf;
-            sc.counters = reinterpret_cast<int*>(base + coff);
-            sc.counter_count = L.groups();
-        }
+        GemvScratch sc = context_gemv_scratch(ctx, pl, b, L, s);
         launch_qgemv(pl, L, w->data(), static_cast<const uint8_t*>(x) + (size_t)r0 * L.k * eb, x_f16, L.k, b,
                      out + r0 * L.n, L.n, EPI_STORE, nullptr, 0, mode, rtz, sc, s);
     }

@@ -113,11 +113,19 @@ struct DeviceBuffer {
     DeviceBuffer& operator=(const DeviceBuffer&) = delete;
 };
 
-// Grow-only scratch arena of a context (split-K partials, counters). Grown
-// outside captured regions; never shrinks while the context lives.
+// Grow-only scratch arena of a context. Layout: [counters | flags | data].
+// The split-K arrival counters sit at a fixed offset and are zero whenever no
+// kernel is running (each launch resets the ones it used), so data written
+// by one op can never be mistaken for counters by the next. Grown outside
+// captured regions; never shrinks while the context lives.
 struct Workspace {
+    static constexpr size_t kCounterInts = 1 << 16;  // one per 32-row group: 2M rows
+    static constexpr size_t kFlagInts = 64;
+    static constexpr size_t kDataOffset = (kCounterInts + kFlagInts) * sizeof(int);
     std::unique_ptr<DeviceBuffer> buf;
-    void* get(size_t bytes, cudaStream_t s);
+    void* get(size_t data_bytes, cudaStream_t s);  // returns the data region
+    int* counters() const { return static_cast<int*>(buf->ptr); }
+    int* flags() const { return static_cast<int*>(buf->ptr) + kCounterInts; }
 };
 
 }  // namespace bc

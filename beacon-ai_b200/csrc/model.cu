@@ -195,6 +195,23 @@ __global__ void unshard_kernel(const float* in, float* out, int parts, int rows,
 
 __global__ void advance_kernel(int* pos) { *pos += 1; }
 
+// Seeded pseudo-random cache rows (splitmix64 of the element index), |v| < 1.
+__global__ void fill_random_kernel(void* dst, int f16, int64_t n, int64_t per_seq, int64_t seq_stride,
+                                   uint64_t seed) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t z = seed + (uint64_t)i * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const float v = (float)(int32_t)(z & 0xFFFFFF) / 8388608.0f - 1.0f;
+    const int64_t off = (i / per_seq) * seq_stride + i % per_seq;
+    if (f16)
+        static_cast<__half*>(dst)[off] = __float2half_rn(v);
+    else
+        static_cast<float*>(dst)[off] = v;
+}
+
 inline unsigned cdiv(int64_t a, int64_t b) { return (unsigned)std::max<int64_t>(1, (a + b - 1) / b); }
 
 }  // namespace
@@ -238,6 +255,7 @@ struct BeaconCudaModel {
     int32_t* h_next = nullptr;
     // graphs: key = batch * 2 + autoregressive
     std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, int> graph_kernels;  // kernel nodes per captured step
     ~BeaconCudaModel();
 };
 
@@ -807,6 +825,17 @@ static void launch_decode_graph(BeaconCudaModel* m, int batch, bool autoregressi
             throw;
         }
         BC_CUDA(cudaStreamEndCapture(s, &g));
+        size_t nn = 0;
+        int kernels = 0;
+        if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn) {
+            std::vector<cudaGraphNode_t> nodes(nn);
+            if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+                for (auto nd : nodes) {
+                    cudaGraphNodeType ty;
+                    if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+                }
+        }
+        m->graph_kernels[key] = kernels;
         cudaGraphExec_t ge = nullptr;
         cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
         cudaGraphDestroy(g);
@@ -933,6 +962,37 @@ int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* m, BeaconCudaStream* s
         *out_avg_us = ms * 1000.0f / (float)(iters * nl);
         const int64_t wbytes = Lp->n * (Lp->k / block_size(Lp->dtype)) * block_bytes(Lp->dtype);
         *out_bytes = (uint64_t)(wbytes + (int64_t)batch * Lp->k * 4 + (int64_t)batch * out_n * 4);
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_fill_kv_random(BeaconCudaModel* m, int32_t n_rows, uint64_t seed) {
+    return guard([&]() -> int32_t {
+        require(m != nullptr, "model_fill_kv_random: null argument");
+        if (n_rows < 0 || n_rows > m->cfg.max_context) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "fill_kv_random: too many rows");
+        set_device(m->ctx);
+        const auto& c = m->cfg;
+        const bool f16 = c.kv_dtype == BEACON_CUDA_DTYPE_F16;
+        const int64_t per_seq = (int64_t)n_rows * m->kd, seq_stride = (int64_t)c.max_context * m->kd;
+        const int64_t n = per_seq * c.max_batch;
+        for (size_t li = 0; li < m->layers.size(); ++li)
+            for (int which = 0; which < 2; ++which) {
+                void* dst = which ? m->layers[li].vc->ptr : m->layers[li].kc->ptr;
+                fill_random_kernel<<<cdiv(n, 256), 256>>>(dst, f16, n, per_seq, seq_stride,
+                                                          seed * 0x9E3779B97F4A7C15ull + li * 2 + which);
+                BC_LAUNCHED("fill_random_kernel");
+            }
+        BC_CUDA(cudaDeviceSynchronize());
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_launches_per_step(BeaconCudaModel* m, int32_t batch, int32_t continuing, int32_t* out) {
+    return guard([&]() -> int32_t {
+        require(m && out, "model_launches_per_step: null argument");
+        auto it = m->graph_kernels.find(batch * 2 + (continuing ? 1 : 0));
+        if (it == m->graph_kernels.end()) invalid("model_launches_per_step: that step has not been captured yet");
+        *out = it->second;
         return BEACON_CUDA_OK;
     });
 }

@@ -438,7 +438,8 @@ int32_t beacon_cuda_op_embedding(BeaconCudaContext* ctx, BeaconCudaStream* strea
             fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "embedding: indices must be I32 or F32");
         const int64_t vocab = weight->shape[0], h = weight->shape[1], seq = indices->numel();
         TensorHolder o(new_tensor(ctx, {seq, h}, BEACON_CUDA_DTYPE_F32));
-        int* err = static_cast<int*>(ctx->ws.get(sizeof(int) * 64, stream->s)) + 32;
+        ctx->ws.get(0, stream->s);
+        int* err = ctx->ws.flags();
         BC_CUDA(cudaMemsetAsync(err, 0, sizeof(int), stream->s));
         if (seq)
             embedding_kernel<<<(unsigned)seq, 256, 0, stream->s>>>(weight->data(), weight->dtype, vocab, h,

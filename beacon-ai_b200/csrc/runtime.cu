@@ -93,7 +93,8 @@ DeviceBuffer::~DeviceBuffer() {
     if (owned && ptr) cudaFree(ptr);
 }
 
-void* Workspace::get(size_t bytes, cudaStream_t s) {
+void* Workspace::get(size_t data_bytes, cudaStream_t s) {
+    const size_t bytes = kDataOffset + data_bytes;
     if (!buf || buf->bytes < bytes) {
         if (s) {
             cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
@@ -107,7 +108,7 @@ void* Workspace::get(size_t bytes, cudaStream_t s) {
         buf = std::make_unique<DeviceBuffer>(want);
         BC_CUDA(cudaMemset(buf->ptr, 0, want));
     }
-    return buf->ptr;
+    return static_cast<uint8_t*>(buf->ptr) + kDataOffset;
 }
 
 void set_device(BeaconCudaContext* ctx) { BC_CUDA(cudaSetDevice(ctx->device)); }
@@ -281,6 +282,14 @@ int32_t beacon_cuda_stream_synchronize(BeaconCudaStream* stream) {
     return guard([&]() -> int32_t {
         require(stream != nullptr, "null stream");
         BC_CUDA(cudaStreamSynchronize(stream->s));
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_stream_handle(BeaconCudaStream* stream, void** out_cuda_stream) {
+    return guard([&]() -> int32_t {
+        require(stream && out_cuda_stream, "beacon_cuda_stream_handle: null argument");
+        *out_cuda_stream = stream->s;
         return BEACON_CUDA_OK;
     });
 }
@@ -487,17 +496,7 @@ int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream
                               static_cast<float*>(o->data()), ctx->numerics);
             } else if (rows > 0) {
                 GemvPlan pl = plan_qgemv(ctx, w->q, (int)rows, mode);
-                GemvScratch sc;
-                if (pl.ksplit > 1) {
-                    size_t pf = (size_t)pl.ksplit * rows * w->q.n_pad;
-                    size_t cbytes = (size_t)w->q.groups() * 4;
-                    size_t coff = (pf * 4 + 255) / 256 * 256;
-                    uint8_t* base = static_cast<uint8_t*>(ctx->ws.get(coff + cbytes, stream->s));
-                    sc.partial = reinterpret_cast<float*>(base);
-                    sc.partial_floats = pf;
-                    sc.counters = reinterpret_cast<int*>(base + coff);
-                    sc.counter_count = w->q.groups();
-                }
+                GemvScratch sc = context_gemv_scratch(ctx, pl, (int)rows, w->q, stream->s);
                 launch_qgemv(pl, w->q, w->data(), x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, K, (int)rows,
                              static_cast<float*>(o->data()), w->q.n, EPI_STORE, nullptr, 0, mode, rtz, sc,
                              stream->s);

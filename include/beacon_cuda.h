@@ -277,6 +277,16 @@ int32_t beacon_cuda_model_decode_step_device(BeaconCudaModel* model, BeaconCudaS
 int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* model, BeaconCudaStream* stream, int32_t slot,
                                          int32_t batch, int32_t iters, float* out_avg_us,
                                          uint64_t* out_bytes);
+/* Fills KV-cache rows [0, n_rows) of every layer and sequence with seeded
+ * pseudo-random values (|v| < 1), standing in for a long prefilled context
+ * when only the decode step is measured: the step's work does not depend on
+ * the cached values. */
+int32_t beacon_cuda_model_fill_kv_random(BeaconCudaModel* model, int32_t n_rows, uint64_t seed);
+/* Kernel launches in one captured decode step (after it has run once). */
+int32_t beacon_cuda_model_launches_per_step(BeaconCudaModel* model, int32_t batch, int32_t continuing,
+                                            int32_t* out_launches);
+/* The cudaStream_t behind a stream handle (as void*). */
+int32_t beacon_cuda_stream_handle(BeaconCudaStream* stream, void** out_cuda_stream);
 /* Bytes of device memory held by the model (weights + KV cache + workspace). */
 int32_t beacon_cuda_model_memory(const BeaconCudaModel* model, uint64_t* out_bytes);
 

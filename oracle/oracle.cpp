@@ -10,6 +10,7 @@
 
 #include "oracle.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -415,6 +416,24 @@ extern "C" int orc_dequantize_to_f32(const uint8_t* data, int dtype, uint64_t n,
     if (dtype == ORC_F16) {
         for (uint64_t i = 0; i < n; ++i) out[i] = orc_f16_to_f32(rd16(data + 2 * i));
         return 0;
+    }
+    // Large tensors: independent block ranges on all threads (results do not
+    // depend on the split).
+    const int64_t bs = orc_block_size(dtype), bb = orc_block_bytes(dtype);
+    const uint64_t chunk_blocks = 1 << 14;
+    if (bs > 1 && n % (uint64_t)bs == 0 && n / (uint64_t)bs > chunk_blocks) {
+        const int64_t nchunks = (int64_t)((n / (uint64_t)bs + chunk_blocks - 1) / chunk_blocks);
+        int err = 0;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) reduction(| : err)
+#endif
+        for (int64_t c = 0; c < nchunks; ++c) {
+            const uint64_t b0 = (uint64_t)c * chunk_blocks;
+            const uint64_t nb = std::min<uint64_t>(chunk_blocks, n / (uint64_t)bs - b0);
+            float* o = out + b0 * (uint64_t)bs;
+            err |= orc_dequantize_to_f32(data + b0 * (uint64_t)bb, dtype, nb * (uint64_t)bs, nibble_order, rtz, o);
+        }
+        return err ? fail("dequant: failed") : 0;
     }
     if (rtz)
         return dequant_values(data, dtype, n, nibble_order, [&](uint64_t i, float v) {
