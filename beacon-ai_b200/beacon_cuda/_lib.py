@@ -98,6 +98,7 @@ SIGNATURES = {
     "beacon_cuda_op_dequantize_to_f16": (_I32, [_P, _P, _P, _PP]),
     "beacon_cuda_op_quantize": (_I32, [_P, _P, _P, _I32, _I32, _PP]),
     "beacon_cuda_quantize_blocks": (_I32, [_P, _P, _P, _I64, _I64, _I32, _I32, _P]),
+    "beacon_cuda_quantized_matvec_noalloc": (_I32, [_P, _P, _P, _I32, _I32, _P]),
     "beacon_cuda_model_create": (_I32, [_P, _P, _PP]),
     "beacon_cuda_model_destroy": (None, [_P]),
     "beacon_cuda_model_set_weight": (_I32, [_P, _I32, _I32, _P, _I32, _I32, _I32]),

@@ -211,6 +211,22 @@ int32_t beacon_cuda_op_dequantize_to_f16(BeaconCudaContext* ctx, BeaconCudaStrea
 int32_t beacon_cuda_op_quantize(BeaconCudaContext* ctx, BeaconCudaStream* stream,
                                 const BeaconCudaTensor* x, int32_t dtype, int32_t nibble_order,
                                 BeaconCudaTensor** out);
+/* Allocation-free quantized matvec; it has no counterpart in the reference.
+ * d_y[b, n] = sum_k dequant(w)[n, k] * d_x[b, k] for b < batch (1..16), with
+ * d_x a contiguous [batch, K] device array (x_dtype F32 or F16) and d_y a
+ * contiguous f32 [batch, N] device array, same numerics as quantized_matmul.
+ * For callers that may not allocate device memory (a fixed arena that owns
+ * all HBM, work overlapping another thread's graph capture, latency-critical
+ * loops): it calls no cudaMalloc/cudaFree. Its split-K scratch is one 2 MiB
+ * array in the library image, held by every GPU that loads the library until
+ * exit. Every call shares it and leaves its contents behind (the arrival
+ * counters are cleared on each call), so calls that overlap on the GPU race:
+ * order them. The first call on a device looks the array up with that device
+ * current; make it outside stream capture. Shapes whose split partial sums do
+ * not fit (batch x rows x K-splits > 520,192) return SHAPE_MISMATCH. */
+int32_t beacon_cuda_quantized_matvec_noalloc(BeaconCudaStream* stream, const BeaconCudaTensor* w,
+                                             const void* d_x, int32_t x_dtype, int32_t batch,
+                                             float* d_y);
 
 /* Device-to-device form of the quantizer: d_x f32 [n_rows, k] -> GGUF block
  * bytes at d_out (n_rows * k / block_size * block_bytes bytes), enqueued on
