@@ -13,6 +13,7 @@
 #include "attention.h"
 #include "common.cuh"
 #include "internal.h"
+#include "kernels.h"
 
 namespace bc {
 
@@ -99,6 +100,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a
     __shared__ float ps[4][G][32];
     __shared__ float wm[4][G], wl[4][G];
     __shared__ float wacc[4][G][D];
+    pdl_trigger();
+    pdl_wait();
     const int bk = blockIdx.x, split = blockIdx.y;
     const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -169,26 +172,34 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a
             ps[warp][g][lane] = p;
         }
         __syncwarp();
+        // phase 2: 8 V rows per round, all loads issued before any use
         const int nk = (int)min((int64_t)32, k1 - kb);
-        for (int j = 0; j < nk; ++j) {
-            const KV* vr = vc + (kb + j) * ks + lane * DPL;
-            float vf[DPL];
-            if (sizeof(KV) == 2) {
+        for (int j0 = 0; j0 < nk; j0 += 8) {
+            float vf[8][DPL];
 #pragma unroll
-                for (int t = 0; t < DPL; t += 2) {
-                    float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr + t));
-                    vf[t] = f.x;
-                    vf[t + 1] = f.y;
+            for (int u = 0; u < 8; ++u) {
+                const bool ok = j0 + u < nk;
+                const KV* vr = vc + (kb + j0 + u) * ks + lane * DPL;
+                if (sizeof(KV) == 2) {
+#pragma unroll
+                    for (int t = 0; t < DPL; t += 2) {
+                        float2 f = ok ? __half22float2(*reinterpret_cast<const __half2*>(vr + t)) : make_float2(0.f, 0.f);
+                        vf[u][t] = f.x;
+                        vf[u][t + 1] = f.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int t = 0; t < DPL; ++t) vf[u][t] = ok ? reinterpret_cast<const float*>(vr)[t] : 0.0f;
                 }
-            } else {
-#pragma unroll
-                for (int t = 0; t < DPL; ++t) vf[t] = reinterpret_cast<const float*>(vr)[t];
             }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float p = ps[warp][g][j];
+            for (int u = 0; u < 8; ++u) {
 #pragma unroll
-                for (int t = 0; t < DPL; ++t) acc[g][t] = fmaf(p, vf[t], acc[g][t]);
+                for (int g = 0; g < G; ++g) {
+                    const float p = (j0 + u < nk) ? ps[warp][g][j0 + u] : 0.0f;
+#pragma unroll
+                    for (int t = 0; t < DPL; ++t) acc[g][t] = fmaf(p, vf[u][t], acc[g][t]);
+                }
             }
         }
         __syncwarp();
@@ -223,36 +234,49 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a
     }
 }
 
-// One warp per (sequence, head): merge the splits and normalise.
+// One CTA (d threads) per (sequence, head): the split weights exp(m_s - M)
+// are computed once in shared memory, then every thread sums its head dim
+// over the splits with all loads independent.
 __global__ void decode_attn_combine_kernel(const DecodeAttnArgs a, int d) {
-    const int64_t hb = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (hb >= (int64_t)a.batch * a.heads) return;
-    float M = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, a.part_m[hb * a.nsplit + s]);
-    float L = 0.0f;
-    for (int s = 0; s < a.nsplit; ++s) {
-        float mm = a.part_m[hb * a.nsplit + s];
-        L += mm == -INFINITY ? 0.0f : a.part_l[hb * a.nsplit + s] * expf(mm - M);
-    }
-    const float inv = 1.0f / L;
-    for (int dd = lane; dd < d; dd += 32) {
-        float o = 0.0f;
-        for (int s = 0; s < a.nsplit; ++s) {
-            float mm = a.part_m[hb * a.nsplit + s];
-            if (mm != -INFINITY) o += a.part_acc[(hb * a.nsplit + s) * d + dd] * expf(mm - M);
+    __shared__ float wsh[kMaxDecodeSplits];
+    __shared__ float inv_l;
+    pdl_trigger();
+    pdl_wait();
+    const int64_t hb = blockIdx.x;
+    const int tid = threadIdx.x, ns = a.nsplit;
+    const float* pm = a.part_m + hb * ns;
+    const float* pl = a.part_l + hb * ns;
+    if (tid < 32) {
+        float M = -INFINITY;
+        for (int s = tid; s < ns; s += 32) M = fmaxf(M, pm[s]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int s = tid; s < ns; s += 32) {
+            const float mm = pm[s];
+            const float wgt = mm == -INFINITY ? 0.0f : expf(mm - M);
+            wsh[s] = wgt;
+            L += pl[s] * wgt;
         }
-        a.out[hb * d + dd] = o * inv;
+        L = warp_sum(L);
+        if (tid == 0) inv_l = 1.0f / L;
+    }
+    __syncthreads();
+    const float* acc = a.part_acc + hb * ns * d;
+    for (int dd = tid; dd < d; dd += blockDim.x) {
+        float o = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < ns; ++s) o = fmaf(acc[(int64_t)s * d + dd], wsh[s], o);
+        a.out[hb * d + dd] = o * inv_l;
     }
 }
 
 template <int D, int G>
-void launch_decode_t(const DecodeAttnArgs& a, cudaStream_t s) {
+void launch_decode_t(const DecodeAttnArgs& a, cudaStream_t s, bool pdl) {
     dim3 grid((unsigned)(a.batch * a.kv_heads), (unsigned)a.nsplit);
     if (a.kv_f16)
-        decode_attn_kernel<D, G, __half><<<grid, 128, 0, s>>>(a);
+        launch_kernel(decode_attn_kernel<D, G, __half>, grid, dim3(128), 0, s, pdl, a);
     else
-        decode_attn_kernel<D, G, float><<<grid, 128, 0, s>>>(a);
+        launch_kernel(decode_attn_kernel<D, G, float>, grid, dim3(128), 0, s, pdl, a);
     BC_LAUNCHED("decode_attn_kernel");
 }
 
@@ -282,22 +306,23 @@ bool decode_attention_supported(int head_dim, int group) {
     return (head_dim == 64 || head_dim == 128) && (group == 1 || group == 2 || group == 4 || group == 8);
 }
 
-void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s) {
+void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s, bool pdl) {
     const int G = a.heads / a.kv_heads;
     if (!decode_attention_supported(a.d, G)) fail(BEACON_CUDA_ERR_SHAPE_MISMATCH, "decode attention: unsupported head shape");
-if (a.d == 128) {
-        if (G == 8) launch_decode_t<128, 8>(a, s);
-        else if (G == 4) launch_decode_t<128, 4>(a, s);
-        else if (G == 2) launch_decode_t<128, 2>(a, s);
-        else launch_decode_t<128, 1>(a, s);
+    if (a.nsplit < 1 || a.nsplit > kMaxDecodeSplits) invalid("decode attention: bad split count");
+    if (a.d == 128) {
+        if (G == 8) launch_decode_t<128, 8>(a, s, pdl);
+        else if (G == 4) launch_decode_t<128, 4>(a, s, pdl);
+        else if (G == 2) launch_decode_t<128, 2>(a, s, pdl);
+        else launch_decode_t<128, 1>(a, s, pdl);
     } else {
-        if (G == 8) launch_decode_t<64, 8>(a, s);
-        else if (G == 4) launch_decode_t<64, 4>(a, s);
-        else if (G == 2) launch_decode_t<64, 2>(a, s);
-        else launch_decode_t<64, 1>(a, s);
+        if (G == 8) launch_decode_t<64, 8>(a, s, pdl);
+        else if (G == 4) launch_decode_t<64, 4>(a, s, pdl);
+        else if (G == 2) launch_decode_t<64, 2>(a, s, pdl);
+        else launch_decode_t<64, 1>(a, s, pdl);
     }
-    const int64_t warps = (int64_t)a.batch * a.heads;
-    decode_attn_combine_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(a, a.d);
+    launch_kernel(decode_attn_combine_kernel, dim3((unsigned)((int64_t)a.batch * a.heads)), dim3(a.d), 0, s, pdl, a,
+                  (int)a.d);
     BC_LAUNCHED("decode_attn_combine_kernel");
 }
 

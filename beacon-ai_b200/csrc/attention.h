@@ -48,8 +48,9 @@ struct DecodeAttnArgs {
     float* part_l;
     float* out;
 };
+constexpr int kMaxDecodeSplits = 64;
 int plan_decode_splits(int batch, int kv_heads, int kv_len, int sm_count, int max_splits);
 bool decode_attention_supported(int head_dim, int group);
-void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s);
+void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s, bool pdl = false);
 
 }  // namespace bc

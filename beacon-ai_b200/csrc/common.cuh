@@ -110,6 +110,14 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while the previous kernel in the stream is still
+// running; before pdl_wait() it may only touch data no earlier kernel writes
+// (weights, its own shared memory). pdl_trigger() lets the next kernel launch.
+// Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 128-bit read-only load that does not allocate in L1 (weights are streamed once).
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
     uint4 r;

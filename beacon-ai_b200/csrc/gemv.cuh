@@ -51,6 +51,8 @@ struct GemvParams {
     float* partial;
     int* counters;
     int rtz;
+    const float* norm_w;  // persistent kernel only: RMSNorm of each x row fused into the staging
+    float norm_eps;
 };
 
 __device__ __forceinline__ float load_x(const GemvParams& p, int b, int64_t kk) {
@@ -438,6 +440,8 @@ __global__ void __launch_bounds__(128) qgemv_kernel(const GemvParams p, const in
     const int t1 = (int)min((int64_t)p.ktiles, (int64_t)t0 + p.tps);
     const int nt = t1 - t0;
     const int span = nt * 256;
+    pdl_trigger();
+    pdl_wait();
     stage_x<FMT, MODE, B>(p, smem, (int64_t)t0 * 256, span);
     __syncthreads();
 
@@ -524,12 +528,13 @@ void launch_qgemv_t(const GemvLaunch& a) {
     p.partial = a.scratch.partial;
     p.counters = a.scratch.counters;
     p.rtz = a.rtz ? 1 : 0;
+    p.norm_w = nullptr;
+    p.norm_eps = 0.0f;
     auto kern = qgemv_kernel<FMT, MODE, B>;
     if (pl.smem > 48 * 1024)
         BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
     const int64_t grid = a.L->groups() * pl.ksplit;
-    kern<<<(unsigned)grid, 128, pl.smem, a.s>>>(p, a.epi);
-    BC_LAUNCHED("qgemv_kernel");
+    launch_kernel(kern, dim3((unsigned)grid), dim3(128), pl.smem, a.s, a.pdl, p, a.epi);
 }
 
 template <int FMT>

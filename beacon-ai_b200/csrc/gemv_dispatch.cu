@@ -1,8 +1,9 @@
-// gemv_dispatch.cu -- split-K planning and format dispatch for the
-// dequant-GEMV kernels (gemv.cuh).
+// gemv_dispatch.cu -- planning and format dispatch for the dequant-GEMV
+// kernels: the tiled split-K kernel (gemv.cuh) and the persistent TMA-fed
+// stream-K kernel (gemv3.cuh).
 #include <algorithm>
 
-#include "gemv.cuh"
+#include "gemv3.cuh"
 
 namespace bc {
 
@@ -46,12 +47,75 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
     }
 }
 
-GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const GemvPlan& pl, int batch, const QLayout& L,
+// The persistent kernel is used for batch <= 8 when at least 2 ring stages
+// per warp and the staged activations fit under the opt-in shared memory, and
+// there are at least as many tiles as warps (every warp range non-empty).
+LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
+    LinearPlan pl;
+    pl.v2 = plan_qgemv(ctx, L, batch, mode);
+    if (batch > 8) return pl;
+    pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : 8;
+    const size_t budget = 200 * 1024;
+    const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad);
+    const size_t tb = (size_t)L.tile_bytes;
+    if (xb + 256 + 2 * kG3Warps * tb > budget) return pl;
+    int stages = (int)std::min<size_t>(6, (budget - xb - 256) / (kG3Warps * tb));
+    const int64_t total_tiles = L.groups() * L.ktiles();
+    const int sms = ctx ? ctx->sm_count : 148;
+    const int64_t nctas = std::min<int64_t>(sms, total_tiles / kG3Warps);
+    if (nctas < 1) return pl;
+    pl.v3 = true;
+    pl.stages = stages;
+    pl.nctas = (int)nctas;
+    pl.total_warps = nctas * kG3Warps;
+    pl.smem = gemv3_bar_bytes(stages) + (size_t)kG3Warps * stages * tb + xb;
+    return pl;
+}
+
+size_t LinearPlan::scratch_floats(int batch, const QLayout& L) const {
+    if (v3) return (size_t)total_warps * 2 * bpad * 32;
+    return v2.ksplit > 1 ? (size_t)v2.ksplit * batch * L.n_pad : 0;
+}
+
+void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
+                   int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,
+                   const GemvScratch& scratch, cudaStream_t s, const float* norm_w, float norm_eps, bool pdl) {
+    GemvLaunch a{&plan.v2, &L, w, x, x_f16, x_ld, batch, y, y_ld, epi, res, res_ld, mode, rtz, scratch, s};
+    a.pdl = pdl;
+    if (!plan.v3) {
+        if (norm_w) invalid("the tiled GEMV has no fused RMSNorm; normalise first");
+        if (plan.v2.ksplit > 1 &&
+            (!scratch.partial || !scratch.counters || scratch.partial_floats < (size_t)plan.v2.ksplit * batch * L.n_pad ||
+             scratch.counter_count < L.groups()))
+            invalid("split-K GEMV launched without enough scratch");
+        switch (L.dtype) {
+            case BEACON_CUDA_DTYPE_Q4_0: return launch_qgemv_q4_0(a);
+            case BEACON_CUDA_DTYPE_Q8_0: return launch_qgemv_q8_0(a);
+            case BEACON_CUDA_DTYPE_Q4_K: return launch_qgemv_q4_k(a);
+            default: fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized GEMV: unsupported block type");
+        }
+    }
+    if (!scratch.partial || !scratch.counters || !scratch.err ||
+        scratch.partial_floats < plan.scratch_floats(batch, L) || scratch.counter_count < L.groups())
+        invalid("stream-K GEMV launched without enough scratch");
+    a.norm_w = norm_w;
+    a.norm_eps = norm_eps;
+    switch (L.dtype) {
+        case BEACON_CUDA_DTYPE_Q4_0: return launch_qgemv3_q4_0(plan, a);
+        case BEACON_CUDA_DTYPE_Q8_0: return launch_qgemv3_q8_0(plan, a);
+        case BEACON_CUDA_DTYPE_Q4_K: return launch_qgemv3_q4_k(plan, a);
+        default: fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized GEMV: unsupported block type");
+    }
+}
+
+GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const LinearPlan& pl, int batch, const QLayout& L,
                                  cudaStream_t s) {
     GemvScratch sc;
-    if (pl.ksplit <= 1) return sc;
+    const size_t pf = pl.scratch_floats(batch, L);
+    ctx->ws.get(pf * sizeof(float), s);  // grows (and zeroes) the arena when needed
+    sc.err = ctx->ws.flags() + 1;
+    if (pf == 0) return sc;
     if ((size_t)L.groups() > Workspace::kCounterInts) shape_err("too many rows for the split-K counters");
-    const size_t pf = (size_t)pl.ksplit * batch * L.n_pad;
     sc.partial = static_cast<float*>(ctx->ws.get(pf * sizeof(float), s));
     sc.partial_floats = pf;
     sc.counters = ctx->ws.counters();
@@ -69,10 +133,10 @@ void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTenso
     const size_t eb = x_f16 ? 2 : 4;
     for (int64_t r0 = 0; r0 < rows; r0 += 16) {
         const int b = (int)std::min<int64_t>(16, rows - r0);
-        GemvPlan pl = plan_qgemv(ctx, L, b, mode);
+        LinearPlan pl = plan_linear(ctx, L, b, mode);
         GemvScratch sc = context_gemv_scratch(ctx, pl, b, L, s);
-        launch_qgemv(pl, L, w->data(), static_cast<const uint8_t*>(x) + (size_t)r0 * L.k * eb, x_f16, L.k, b,
-                     out + r0 * L.n, L.n, EPI_STORE, nullptr, 0, mode, rtz, sc, s);
+        launch_linear(pl, L, w->data(), static_cast<const uint8_t*>(x) + (size_t)r0 * L.k * eb, x_f16, L.k, b,
+                      out + r0 * L.n, L.n, EPI_STORE, nullptr, 0, mode, rtz, sc, s);
     }
 }
 

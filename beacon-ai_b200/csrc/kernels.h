@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <utility>
 
 #include "internal.h"
 
@@ -20,6 +21,7 @@ struct GemvScratch {
     int* counters = nullptr;
     size_t partial_floats = 0;
     int64_t counter_count = 0;
+    int* err = nullptr;  // set by a kernel whose bounded wait gave up
 };
 
 struct GemvPlan {
@@ -57,10 +59,50 @@ struct GemvLaunch {
     bool rtz;
     GemvScratch scratch;
     cudaStream_t s;
+    const float* norm_w = nullptr;  // fused RMSNorm weight (persistent kernel only)
+    float norm_eps = 0.0f;
+    bool pdl = false;               // launch with programmatic stream serialisation
 };
+
+// cudaLaunchKernelEx with programmatic stream serialisation when `pdl`.
+template <typename... KArgs, typename... Args>
+void launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                   Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cuda_check(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), "cudaLaunchKernelEx");
+}
 void launch_qgemv_q4_0(const GemvLaunch& a);
 void launch_qgemv_q8_0(const GemvLaunch& a);
 void launch_qgemv_q4_k(const GemvLaunch& a);
+
+// The persistent TMA-fed GEMV (gemv3.cuh) for batch <= 8 when its ring and the
+// staged activations fit in shared memory; otherwise the tiled GEMV above.
+struct LinearPlan {
+    bool v3 = false;
+    GemvPlan v2;
+    int nctas = 0, stages = 0, bpad = 1;
+    size_t smem = 0;
+    int64_t total_warps = 0;
+    size_t scratch_floats(int batch, const QLayout& L) const;
+};
+LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode);
+// norm_w (persistent plan only): y = W rmsnorm(x, norm_w, norm_eps).
+void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
+                   int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,
+                   const GemvScratch& scratch, cudaStream_t s, const float* norm_w = nullptr, float norm_eps = 0.0f,
+                   bool pdl = false);
+void launch_qgemv3_q4_0(const LinearPlan& pl, const GemvLaunch& a);
+void launch_qgemv3_q8_0(const LinearPlan& pl, const GemvLaunch& a);
+void launch_qgemv3_q4_k(const LinearPlan& pl, const GemvLaunch& a);
 
 // Quantized layout kernels (quant.cu). row_map (device, one entry per tiled
 // row, optional): raw row to copy, -1 = zero row, -2 = leave the row as is.
@@ -71,7 +113,8 @@ void launch_quantize(int32_t dtype, const float* x, int64_t n_rows, int64_t k, i
                      uint8_t* raw, cudaStream_t s);
 
 // Split-K scratch carved from the context workspace (fixed zeroed counters).
-GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const GemvPlan& pl, int batch, const QLayout& L,
+struct LinearPlan;
+GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const LinearPlan& pl, int batch, const QLayout& L,
                                  cudaStream_t s);
 
 // Prefill-sized quantized matmul (rows > 16): out[rows, N] = x @ W^T.

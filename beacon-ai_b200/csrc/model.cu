@@ -16,12 +16,14 @@
 // greedy argmax with the reference's tie rule (sampling.rs:60-66).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
 #include <string>
 #include <vector>
 
+#include "argmax.h"
 #include "attention.h"
 #include "common.cuh"
 #include "internal.h"
@@ -40,6 +42,8 @@ __device__ __forceinline__ int read_pos(const int* pos_ptr, int pos_imm) { retur
 // h[row] = E[tok[row]] (f32). Out-of-range ids write zeros and raise *err.
 __global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hid, const int32_t* tok, float* h,
                              int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int row = blockIdx.x;
     const int32_t t = tok[row];
     const bool ok = t >= 0 && t < vocab;
@@ -52,20 +56,45 @@ __global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hi
     }
 }
 
-// ops.rs:77-93 per row; w is f32
-__global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, int64_t d, float eps) {
-    __shared__ float sh[32];
+// ops.rs:77-93 per row; w is f32. d % 4 == 0 and d <= 4 * 256 * kRmsVec: each
+// thread keeps its float4s in registers, so the row is read once.
+constexpr int kRmsVec = 8;
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                           float* __restrict__ out, int64_t d, float eps) {
+    __shared__ float sh[8];
+    pdl_trigger();
+    pdl_wait();
     const int64_t row = blockIdx.x;
-    const float* xr = x + row * d;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * d);
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    const int n4 = (int)(d / 4);
+    float4 v[kRmsVec];
     float ss = 0.0f;
-    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int i = 0; i < kRmsVec; ++i) {
+        const int j = threadIdx.x + i * 256;
+        v[i] = j < n4 ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss = fmaf(v[i].x, v[i].x, ss);
+        ss = fmaf(v[i].y, v[i].y, ss);
+        ss = fmaf(v[i].z, v[i].z, ss);
+        ss = fmaf(v[i].w, v[i].w, ss);
+    }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
     __syncthreads();
     float t = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += sh[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += sh[i];
     const float inv = 1.0f / sqrtf(t / (float)d + eps);
-    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) out[row * d + i] = xr[i] * inv * w[i];
+    float4* o = reinterpret_cast<float4*>(out + row * d);
+#pragma unroll
+    for (int i = 0; i < kRmsVec; ++i) {
+        const int j = threadIdx.x + i * 256;
+        if (j < n4) {
+            const float4 g = wr[j];
+            o[j] = make_float4(v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w);
+        }
+    }
 }
 
 // cos/sin table [max_ctx][D/2] with the CPU formula (ops.rs:131-135)
@@ -88,6 +117,8 @@ template <typename KV>
 __global__ void qkv_post_kernel(const float* qkv, float* q, KV* kc, KV* vc, const float* cs, const float* sn,
                                 int rows, int qd, int kd, int d, int64_t cache_sb, const int* pos_ptr, int pos_imm,
                                 int pos_step, int seq_step, int max_ctx, int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.y;
     const int pos0 = read_pos(pos_ptr, pos_imm);
     const int pos = pos0 + r * pos_step;
@@ -122,70 +153,10 @@ __global__ void qkv_post_kernel(const float* qkv, float* q, KV* kc, KV* vc, cons
     }
 }
 
-// Greedy argmax per row (rule of sampling.rs:60-66, see ops.cu). logits are
-// [rows][n] or, with parts > 1, [parts][rows][n/parts] (all-gathered shards).
-__global__ void argmax_rows_kernel(const float* x, int64_t n, int parts, int rows, int32_t* out, int32_t* out2) {
-    __shared__ int64_t shi[32];
-    __shared__ float shv[32];
-    const int row = blockIdx.x;
-    const int64_t per = n / parts;
-    auto at = [&](int64_t i) -> float {
-        const int64_t p = i / per, j = i - p * per;
-        return x[(p * rows + row) * per + j];
-    };
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-    int64_t last_nan = -1;
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
-        if (isnan(at(i))) last_nan = i;
-    for (int o = 16; o; o >>= 1) last_nan = max(last_nan, __shfl_xor_sync(0xffffffffu, last_nan, o));
-    if (l == 0) shi[w] = last_nan;
-    __syncthreads();
-    last_nan = -1;
-    for (int i = 0; i < nw; ++i) last_nan = max(last_nan, shi[i]);
-    __syncthreads();
-    int64_t result;
-    if (last_nan == n - 1) {
-        result = n - 1;
-    } else {
-        float bv = -INFINITY;
-        int64_t bi = -1;
-        for (int64_t i = last_nan + 1 + threadIdx.x; i < n; i += blockDim.x) {
-            float c = at(i);
-            if (bi < 0 || c > bv || (c == bv && i > bi)) {
-                bv = c;
-                bi = i;
-            }
-        }
-        for (int o = 16; o; o >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (l == 0) {
-            shv[w] = bv;
-            shi[w] = bi;
-        }
-        __syncthreads();
-        bv = -INFINITY;
-        bi = -1;
-        for (int i = 0; i < nw; ++i)
-            if (shi[i] >= 0 && (bi < 0 || shv[i] > bv || (shv[i] == bv && shi[i] > bi))) {
-                bv = shv[i];
-                bi = shi[i];
-            }
-        result = bi;
-    }
-    if (threadIdx.x == 0) {
-        out[row] = (int32_t)result;
-        if (out2) out2[row] = (int32_t)result;
-    }
-}
-
 // [parts][rows][per] -> [rows][parts*per]
 __global__ void unshard_kernel(const float* in, float* out, int parts, int rows, int64_t per) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t n = (int64_t)parts * rows * per;
     if (i >= n) return;
@@ -193,7 +164,11 @@ __global__ void unshard_kernel(const float* in, float* out, int parts, int rows,
     out[r * (parts * per) + p * per + j] = in[i];
 }
 
-__global__ void advance_kernel(int* pos) { *pos += 1; }
+__global__ void advance_kernel(int* pos) {
+    pdl_trigger();
+    pdl_wait();
+    *pos += 1;
+}
 
 // Seeded pseudo-random cache rows (splitmix64 of the element index), |v| < 1.
 __global__ void fill_random_kernel(void* dst, int f16, int64_t n, int64_t per_seq, int64_t seq_stride,
@@ -250,6 +225,9 @@ struct BeaconCudaModel {
     std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
     int attn_nsplit = 1;
     float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
+    std::unique_ptr<bc::DeviceBuffer> argmax_buf;
+    bool pdl = true;  // programmatic dependent launch between the step's kernels
+    bc::ArgmaxSummary* argmax_scratch = nullptr;
     // host staging (pinned)
     int32_t* h_stage = nullptr;  // [0] = position, [1..] tokens
     int32_t* h_next = nullptr;
@@ -270,15 +248,36 @@ void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x,
             int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s) {
     for (int r0 = 0; r0 < rows; r0 += 16) {
         const int b = std::min(16, rows - r0);
-        GemvPlan pl = plan_qgemv(m->ctx, L, b, gemv_mode(m));
-        launch_qgemv(pl, L, w, x + (int64_t)r0 * x_ld, false, x_ld, b, y + (int64_t)r0 * y_ld, y_ld, epi,
-                     res ? res + (int64_t)r0 * res_ld : nullptr, res_ld, gemv_mode(m), gemv_rtz(m), m->gsc, s);
+        LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
+        launch_linear(pl, L, w, x + (int64_t)r0 * x_ld, false, x_ld, b, y + (int64_t)r0 * y_ld, y_ld, epi,
+                      res ? res + (int64_t)r0 * res_ld : nullptr, res_ld, gemv_mode(m), gemv_rtz(m), m->gsc, s,
+                      nullptr, 0.0f, m->pdl);
     }
 }
 
 void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int rows, cudaStream_t s) {
-    rmsnorm_rows_kernel<<<rows, 256, 0, s>>>(x, w, out, m->cfg.hidden_size, m->cfg.rms_norm_eps);
-    BC_LAUNCHED("rmsnorm_rows_kernel");
+    launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, s, m->pdl, x, w, out, (int64_t)m->cfg.hidden_size,
+                  m->cfg.rms_norm_eps);
+}
+
+// y = W rmsnorm(x, norm_w): the norm rides in the persistent GEMV's staging
+// when every row chunk takes that kernel, otherwise it runs on its own first.
+void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, const float* norm_w, int rows,
+                   float* y, int64_t y_ld, int epi, cudaStream_t s) {
+    const int64_t hid = m->cfg.hidden_size;
+    bool fused = true;
+    for (int r0 = 0; r0 < rows && fused; r0 += 16) fused = plan_linear(m->ctx, L, std::min(16, rows - r0), gemv_mode(m)).v3;
+    if (!fused) {
+        rmsnorm(m, x, norm_w, m->xn, rows, s);
+        linear(m, L, w, m->xn, hid, rows, y, y_ld, epi, nullptr, 0, s);
+        return;
+    }
+    for (int r0 = 0; r0 < rows; r0 += 16) {
+        const int b = std::min(16, rows - r0);
+        LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
+        launch_linear(pl, L, w, x + (int64_t)r0 * hid, false, hid, b, y + (int64_t)r0 * y_ld, y_ld, epi, nullptr, 0,
+                      gemv_mode(m), gemv_rtz(m), m->gsc, s, norm_w, m->cfg.rms_norm_eps, m->pdl);
+    }
 }
 
 // One pass of the decoder over `rows` rows that are either B sequences at
@@ -292,24 +291,23 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
     const int64_t cache_sb = (int64_t)c.max_context * m->kd;
     for (int li = 0; li < c.num_layers; ++li) {
         LayerW& L = m->layers[li];
-        rmsnorm(m, m->h, static_cast<const float*>(L.attn_norm->ptr), m->xn, rows, s);
-        linear(m, m->Lqkv, L.wqkv->ptr, m->xn, hid, rows, m->qkv, m->qkv_n, EPI_STORE, nullptr, 0, s);
+        normed_linear(m, m->Lqkv, L.wqkv->ptr, m->h, static_cast<const float*>(L.attn_norm->ptr), rows, m->qkv,
+                      m->qkv_n, EPI_STORE, s);
         {
             dim3 grid(cdiv(m->qd / 2 + m->kd, 256), rows);
             const int pos_step = decode ? 0 : 1, seq_step = decode ? 1 : 0;
+            const float* cs = static_cast<const float*>(m->rope_cs->ptr);
+            const float* sn = static_cast<const float*>(m->rope_sn->ptr);
             if (f16kv)
-                qkv_post_kernel<__half><<<grid, 256, 0, s>>>(
-                    m->qkv, m->q, static_cast<__half*>(L.kc->ptr), static_cast<__half*>(L.vc->ptr),
-                    static_cast<const float*>(m->rope_cs->ptr), static_cast<const float*>(m->rope_sn->ptr), rows,
-                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step, c.max_context,
-                    m->err_dev);
+                launch_kernel(qkv_post_kernel<__half>, grid, dim3(256), 0, s, m->pdl, (const float*)m->qkv, m->q,
+                              static_cast<__half*>(L.kc->ptr), static_cast<__half*>(L.vc->ptr), cs, sn, rows,
+                              (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step,
+                              (int)c.max_context, m->err_dev);
             else
-                qkv_post_kernel<float><<<grid, 256, 0, s>>>(
-                    m->qkv, m->q, static_cast<float*>(L.kc->ptr), static_cast<float*>(L.vc->ptr),
-                    static_cast<const float*>(m->rope_cs->ptr), static_cast<const float*>(m->rope_sn->ptr), rows,
-                    (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step, c.max_context,
-                    m->err_dev);
-            BC_LAUNCHED("qkv_post_kernel");
+                launch_kernel(qkv_post_kernel<float>, grid, dim3(256), 0, s, m->pdl, (const float*)m->qkv, m->q,
+                              static_cast<float*>(L.kc->ptr), static_cast<float*>(L.vc->ptr), cs, sn, rows,
+                              (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step,
+                              (int)c.max_context, m->err_dev);
         }
         const float scale = 1.0f / sqrtf((float)D);  // engine.rs:415
         if (decode) {
@@ -332,7 +330,7 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.part_m = m->pm;
             a.part_l = m->pl;
             a.out = m->attn;
-            launch_decode_attention(a, s);
+            launch_decode_attention(a, s, m->pdl);
         } else {
             AttnRowsArgs a{};
             a.q = m->q;
@@ -365,15 +363,15 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
         linear(m, m->Lo, L.wo->ptr, m->attn, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE, r0 ? m->h : nullptr,
                hid, s);
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
-        rmsnorm(m, m->h, static_cast<const float*>(L.ffn_norm->ptr), m->xn, rows, s);
-        linear(m, m->Lgu, L.wgu->ptr, m->xn, hid, rows, m->ffn, m->f_loc, EPI_SWIGLU, nullptr, 0, s);
+        normed_linear(m, m->Lgu, L.wgu->ptr, m->h, static_cast<const float*>(L.ffn_norm->ptr), rows, m->ffn, m->f_loc,
+                      EPI_SWIGLU, s);
         linear(m, m->Ld, L.wd->ptr, m->ffn, m->f_loc, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE, r0 ? m->h : nullptr,
                hid, s);
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
     }
     // final norm + lm_head (engine.rs:230-234)
-    rmsnorm(m, m->h, static_cast<const float*>(m->final_norm->ptr), m->xn, rows, s);
-    linear(m, m->Llm, m->wlm->ptr, m->xn, hid, rows, m->logits_loc, m->v_loc, EPI_STORE, nullptr, 0, s);
+    normed_linear(m, m->Llm, m->wlm->ptr, m->h, static_cast<const float*>(m->final_norm->ptr), rows, m->logits_loc,
+                  m->v_loc, EPI_STORE, s);
     if (m->tp > 1) {
         comm_all_gather(m->ctx, m->logits_loc, m->logits_all, (size_t)rows * m->v_loc, s);
     }
@@ -381,30 +379,22 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
 
 // logits [rows][V] (unsharded) and argmax -> next (and tok, for the next step)
 void finish_logits(BeaconCudaModel* m, int rows, bool need_full_logits, bool feed_back, cudaStream_t s) {
-    const int64_t V = m->cfg.vocab_size;
     const float* src = m->tp > 1 ? m->logits_all : m->logits_loc;
-    argmax_rows_kernel<<<rows, 256, 0, s>>>(src, m->v_loc * m->tp, m->tp, rows, m->next, feed_back ? m->tok : nullptr);
-    BC_LAUNCHED("argmax_rows_kernel");
-    if (need_full_logits && m->tp > 1) {
-        unshard_kernel<<<cdiv((int64_t)rows * m->v_loc * m->tp, 256), 256, 0, s>>>(m->logits_all, m->logits, m->tp, rows,
-                                                                                    m->v_loc);
-        BC_LAUNCHED("unshard_kernel");
-    }
-    (void)V;
+    launch_argmax(src, m->v_loc, m->tp, rows, m->next, feed_back ? m->tok : nullptr, m->argmax_scratch, s, m->pdl);
+    if (need_full_logits && m->tp > 1)
+        launch_kernel(unshard_kernel, dim3(cdiv((int64_t)rows * m->v_loc * m->tp, 256)), dim3(256), 0, s, m->pdl,
+                      (const float*)m->logits_all, m->logits, (int)m->tp, rows, (int64_t)m->v_loc);
 }
 
 float* full_logits(BeaconCudaModel* m) { return m->tp > 1 ? m->logits : m->logits_loc; }
 
 void decode_body(BeaconCudaModel* m, int batch, bool autoregressive, cudaStream_t s) {
-    embed_kernel<<<batch, 256, 0, s>>>(m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, m->cfg.vocab_size,
-                                       m->cfg.hidden_size, m->tok, m->h, m->err_dev);
-    BC_LAUNCHED("embed_kernel");
+    launch_kernel(embed_kernel, dim3(batch), dim3(256), 0, s, m->pdl, (const void*)m->embed->ptr,
+                  (int)(m->embed_dtype == BEACON_CUDA_DTYPE_F16), (int64_t)m->cfg.vocab_size,
+                  (int64_t)m->cfg.hidden_size, (const int32_t*)m->tok, m->h, m->err_dev);
     run_layers(m, batch, true, m->pos_dev, 0, s);
     finish_logits(m, batch, m->tp > 1, autoregressive, s);
-    if (autoregressive) {
-        advance_kernel<<<1, 1, 0, s>>>(m->pos_dev);
-        BC_LAUNCHED("advance_kernel");
-    }
+    if (autoregressive) launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, m->pdl, m->pos_dev);
 }
 
 void check_ready(const BeaconCudaModel* m) {
@@ -507,6 +497,8 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
         if (c.num_heads % c.num_kv_heads) shape_err("model_create: num_heads % num_kv_heads != 0");
         if (c.num_heads * c.head_dim != c.hidden_size) shape_err("model_create: num_heads * head_dim != hidden_size");
         if (c.head_dim % 32) shape_err("model_create: head_dim must be a multiple of 32");
+        if (c.hidden_size % 4 || c.hidden_size > 4 * 256 * kRmsVec)
+            shape_err("model_create: hidden_size must be a multiple of 4 and at most 8192");
         if (c.kv_dtype != BEACON_CUDA_DTYPE_F16 && c.kv_dtype != BEACON_CUDA_DTYPE_F32)
             fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "model_create: kv_dtype must be F16 or F32");
         if (c.numerics < 0 || c.numerics > 2) invalid("model_create: unknown numerics");
@@ -518,6 +510,7 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
             shape_err("model_create: kv heads, intermediate size and vocab must divide by tp_size");
         auto m = std::make_unique<BeaconCudaModel>();
         m->ctx = ctx;
+        if (std::getenv("BEACON_CUDA_NO_PDL")) m->pdl = false;
         m->cfg = c;
         m->tp = tp;
         m->rank = c.tp_rank;
@@ -585,6 +578,9 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
         m->pacc = static_cast<float*>(m->attn_buf->ptr);
         m->pm = m->pacc + pa * c.head_dim;
         m->pl = m->pm + pa;
+        const size_t na = argmax_scratch_count(m->v_loc, tp, (int)R);
+        m->argmax_buf = std::make_unique<DeviceBuffer>(na * sizeof(ArgmaxSummary));
+        m->argmax_scratch = static_cast<ArgmaxSummary*>(m->argmax_buf->ptr);
         BC_CUDA(cudaMallocHost(&m->h_stage, (size_t)(R + 1) * 4));
         BC_CUDA(cudaMallocHost(&m->h_next, (size_t)R * 4));
         BC_CUDA(cudaDeviceSynchronize());
@@ -725,21 +721,22 @@ int32_t beacon_cuda_model_set_weight(BeaconCudaModel* m, int32_t layer, int32_t 
         for (const QLayout* Lp : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Ld, &m->Llm}) {
             if (Lp->n == 0) continue;
             for (int b = 1; b <= 16; ++b) {
-                GemvPlan pl = plan_qgemv(m->ctx, *Lp, b, gemv_mode(m));
-                if (pl.ksplit > 1) need_p = std::max(need_p, (size_t)pl.ksplit * b * Lp->n_pad);
+                LinearPlan pl = plan_linear(m->ctx, *Lp, b, gemv_mode(m));
+                need_p = std::max(need_p, pl.scratch_floats(b, *Lp));
             }
             need_c = std::max(need_c, Lp->groups());
         }
-        if (need_p > m->gsc.partial_floats || need_c > m->gsc.counter_count) {
+        if (need_p > m->gsc.partial_floats || need_c > m->gsc.counter_count || !m->gsc.err) {
             const size_t pf = std::max(need_p, m->gsc.partial_floats), cc = (size_t)std::max(need_c, m->gsc.counter_count);
             const size_t coff = (pf * 4 + 255) / 256 * 256;
-            auto buf = std::make_unique<DeviceBuffer>(coff + cc * 4);
-            BC_CUDA(cudaMemset(buf->ptr, 0, coff + cc * 4));
+            auto buf = std::make_unique<DeviceBuffer>(coff + cc * 4 + 256);
+            BC_CUDA(cudaMemset(buf->ptr, 0, coff + cc * 4 + 256));
             m->gemv_buf = std::move(buf);
             m->gsc.partial = static_cast<float*>(m->gemv_buf->ptr);
             m->gsc.partial_floats = pf;
             m->gsc.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(m->gemv_buf->ptr) + coff);
             m->gsc.counter_count = (int64_t)cc;
+            m->gsc.err = reinterpret_cast<int*>(static_cast<uint8_t*>(m->gemv_buf->ptr) + coff + cc * 4);
         }
         return BEACON_CUDA_OK;
     });
@@ -1008,7 +1005,7 @@ int32_t beacon_cuda_model_memory(const BeaconCudaModel* m, uint64_t* out_bytes) 
             add(L.attn_norm); add(L.ffn_norm); add(L.wqkv); add(L.wo); add(L.wgu); add(L.wd); add(L.kc); add(L.vc);
         }
         add(m->embed); add(m->final_norm); add(m->wlm); add(m->rope_cs); add(m->rope_sn); add(m->act);
-        add(m->gemv_buf); add(m->attn_buf);
+        add(m->gemv_buf); add(m->attn_buf); add(m->argmax_buf);
         *out_bytes = t;
         return BEACON_CUDA_OK;
     });

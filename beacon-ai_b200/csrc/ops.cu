@@ -7,6 +7,7 @@
 #include <string>
 #include <vector>
 
+#include "argmax.h"
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
@@ -147,67 +148,6 @@ __global__ void kv_write_kernel(void* cache, int32_t ct, const void* nw, int32_t
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     st_any(cache, ct, pos * row + i, ld_any(nw, nt, i));
-}
-
-// Greedy argmax with the reference's rule (sampling.rs:60-66): the scan keeps
-// `best` only while v[best] > v[i], so ties and NaNs move it to the later
-// index. Equivalent closed form: let j be the last NaN; the answer is n-1 if
-// j == n-1, else the last index of the maximum of v[j+1 ..].
-__global__ void argmax_kernel(const float* x, int64_t d, int32_t* out) {
-    __shared__ int64_t shi[32];
-    __shared__ float shv[32];
-    const int64_t row = blockIdx.x;
-    const float* v = x + row * d;
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-    int64_t last_nan = -1;
-    for (int64_t i = threadIdx.x; i < d; i += blockDim.x)
-        if (isnan(v[i])) last_nan = i;
-    for (int o = 16; o; o >>= 1) last_nan = max(last_nan, __shfl_xor_sync(0xffffffffu, last_nan, o));
-    if (l == 0) shi[w] = last_nan;
-    __syncthreads();
-    last_nan = -1;
-    for (int i = 0; i < nw; ++i) last_nan = max(last_nan, shi[i]);
-    __syncthreads();
-    if (d == 0) {
-        if (threadIdx.x == 0) out[row] = 0;
-        return;
-    }
-    if (last_nan == d - 1) {
-        if (threadIdx.x == 0) out[row] = (int32_t)(d - 1);
-        return;
-    }
-    float bv = -INFINITY;
-    int64_t bi = -1;
-    for (int64_t i = last_nan + 1 + threadIdx.x; i < d; i += blockDim.x) {
-        float c = v[i];
-        if (bi < 0 || c > bv || (c == bv && i > bi)) {
-            bv = c;
-            bi = i;
-        }
-    }
-    for (int o = 16; o; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    if (l == 0) {
-        shv[w] = bv;
-        shi[w] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float best = -INFINITY;
-        int64_t besti = -1;
-        for (int i = 0; i < nw; ++i)
-            if (shi[i] >= 0 && (besti < 0 || shv[i] > best || (shv[i] == best && shi[i] > besti))) {
-                best = shv[i];
-                besti = shi[i];
-            }
-        out[row] = (int32_t)besti;
-    }
 }
 
 // ops.rs:16-30 (a [m,k] x b [k,n]), 16x16 shared-memory tiles
@@ -511,10 +451,14 @@ int32_t beacon_cuda_op_argmax(BeaconCudaContext* ctx, BeaconCudaStream* stream, 
         const int64_t d = logits->shape.empty() ? 1 : logits->shape.back();
         const int64_t rows = logits->shape.size() <= 1 ? 1 : logits->numel() / std::max<int64_t>(d, 1);
         TensorHolder o(new_tensor(ctx, {rows}, BEACON_CUDA_DTYPE_I32));
-        if (rows)
-            argmax_kernel<<<(unsigned)rows, 256, 0, stream->s>>>(static_cast<const float*>(logits->data()), d,
-                                                                 static_cast<int32_t*>(o.t->data()));
-        BC_LAUNCHED("argmax_kernel");
+        if (rows && d == 0) {
+            BC_CUDA(cudaMemsetAsync(o.t->data(), 0, (size_t)rows * 4, stream->s));  // empty -> 0 (sampling.rs:65)
+        } else if (rows) {
+            auto* scratch = static_cast<ArgmaxSummary*>(
+                ctx->ws.get(argmax_scratch_count(d, 1, (int)rows) * sizeof(ArgmaxSummary), stream->s));
+            launch_argmax(static_cast<const float*>(logits->data()), d, 1, (int)rows,
+                          static_cast<int32_t*>(o.t->data()), nullptr, scratch, stream->s);
+        }
         return o.release();
     });
 }

@@ -495,11 +495,11 @@ int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream
                 dense_qmatmul(ctx, stream->s, w, x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, rows,
                               static_cast<float*>(o->data()), ctx->numerics);
             } else if (rows > 0) {
-                GemvPlan pl = plan_qgemv(ctx, w->q, (int)rows, mode);
+                LinearPlan pl = plan_linear(ctx, w->q, (int)rows, mode);
                 GemvScratch sc = context_gemv_scratch(ctx, pl, (int)rows, w->q, stream->s);
-                launch_qgemv(pl, w->q, w->data(), x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, K, (int)rows,
-                             static_cast<float*>(o->data()), w->q.n, EPI_STORE, nullptr, 0, mode, rtz, sc,
-                             stream->s);
+                launch_linear(pl, w->q, w->data(), x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, K, (int)rows,
+                              static_cast<float*>(o->data()), w->q.n, EPI_STORE, nullptr, 0, mode, rtz, sc,
+                              stream->s);
             }
         } catch (...) {
             delete o;
