@@ -270,6 +270,265 @@ __global__ void decode_attn_combine_kernel(const DecodeAttnArgs a, int d) {
     }
 }
 
+// Decode attention over an f16 KV cache ------------------------------------------
+// One CTA (4 warps) per (sequence, KV head, split of the keys). The split's
+// key and value rows are staged in shared memory by 1-D bulk copies, 64 keys
+// per stage in a ring of up to 4 stages; every row except the decoded token's
+// (written by the previous kernel) is requested before the kernel waits on its
+// predecessor, so the cache stream overlaps the preceding GEMV. Phase 1: each
+// key is taken by a lane pair of one warp (half the head dims each) for all G
+// query heads of the KV head; phase 2: lanes over head dims accumulate p * v,
+// with an online softmax across stages (engine.rs:415-440). The splits of a
+// (sequence, KV head) are merged in split order by the last of its CTAs to
+// finish (arrival counter), so no separate combine kernel runs.
+constexpr int kAttKeys = 64;
+constexpr int kAttStages = 4;
+constexpr int kAttThreads = 128;
+
+template <int D>
+struct AttLayout {
+    static constexpr int kRow = 2 * D + 16;  // padded key row: 8 lanes' rows fall in distinct banks
+    static constexpr int vRow = 2 * D;
+    static constexpr int stage = kAttKeys * (kRow + vRow);
+    static constexpr size_t smem = (size_t)kAttStages * stage;
+};
+
+template <int D, int G>
+__global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const DecodeAttnArgs a) {
+    using Lay = AttLayout<D>;
+    constexpr int DPL = D / 32;  // phase 2: head dims per lane
+    constexpr int HD = D / 2;    // phase 1: head dims per lane of a pair
+    static_assert(kAttThreads == 2 * kAttKeys, "one thread per staged row");
+    extern __shared__ __align__(128) uint8_t att_smem[];
+    __shared__ __align__(8) uint64_t bars[kAttStages];
+    __shared__ __align__(16) float qs[G][D];
+    __shared__ __align__(16) float ps[kAttKeys][G];
+    __shared__ float corr_s[G], m_s[G], l_s[G];
+    __shared__ int flag_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bk = blockIdx.x, split = blockIdx.y;
+    const int b = bk / a.kv_heads, kvh = bk - b * a.kv_heads;
+    // the key range: the position counter is not written during a step
+    const int kv_len = max(1, min(a.max_kv, a.pos_ptr ? *a.pos_ptr + 1 : a.kv_len));
+    const int chunk = (kv_len + a.nsplit - 1) / a.nsplit;
+    const int k0 = min(kv_len, split * chunk), k1 = min(kv_len, k0 + chunk);
+    const int nkeys = k1 - k0;
+    const int nsteps = (nkeys + kAttKeys - 1) / kAttKeys;
+    const int cur = kv_len - 1;  // the decoded token's row
+    const int64_t ks = (int64_t)a.kv_heads * D;
+    const __half* kc = reinterpret_cast<const __half*>(a.k_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    const __half* vc = reinterpret_cast<const __half*>(a.v_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    // thread t copies row t & 63 of a step: its key (t < 64) or its value row
+    auto step_bytes = [&](int s) { return (uint32_t)min(kAttKeys, nkeys - s * kAttKeys) * (uint32_t)(4 * D); };
+    // mode 0: every row of step s; 1: all but the decoded token's; 2: only it
+    auto issue = [&](int s, int mode) {
+        const int r = tid & (kAttKeys - 1);
+        const int key = k0 + s * kAttKeys + r;
+        if (key >= k1 || (mode == 1 && key == cur) || (mode == 2 && key != cur)) return;
+        uint8_t* base = att_smem + (size_t)(s % kAttStages) * Lay::stage;
+        if (tid < kAttKeys)
+            bulk_g2s(base + r * Lay::kRow, kc + key * ks, 2 * D, &bars[s % kAttStages]);
+        else
+            bulk_g2s(base + kAttKeys * Lay::kRow + r * Lay::vRow, vc + key * ks, 2 * D, &bars[s % kAttStages]);
+    };
+    const int npre = min(kAttStages, nsteps);
+    if (tid == 0) {
+        for (int s = 0; s < kAttStages; ++s) mbar_init(&bars[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int s = 0; s < npre; ++s) mbar_expect_tx(&bars[s], step_bytes(s));
+    }
+    __syncthreads();
+    for (int s = 0; s < npre; ++s) issue(s, 1);
+    pdl_trigger();
+    pdl_wait();
+    if (cur >= k0 && cur < k1 && (cur - k0) / kAttKeys < npre) issue((cur - k0) / kAttKeys, 2);
+    for (int i = tid; i < G * D; i += kAttThreads) {
+        const int g = i / D, dd = i - g * D;
+        qs[g][dd] = a.q[((int64_t)b * a.heads + kvh * G + g) * D + dd] * a.scale;
+    }
+    if (tid < G) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.0f;
+    }
+    float acc[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[g][j] = 0.0f;
+    __syncthreads();
+    int s = 0;
+    bool failed = false;
+    for (; s < nsteps; ++s) {
+        const int st = s % kAttStages;
+        const bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((s / kAttStages) & 1));
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        const int n = min(kAttKeys, k1 - (k0 + s * kAttKeys));
+        const uint8_t* kbase = att_smem + (size_t)st * Lay::stage;
+        const uint8_t* vbase = kbase + kAttKeys * Lay::kRow;
+        {  // phase 1: scores of key r for the G heads
+            const int r = warp * 16 + (lane & 15), h = lane >> 4;
+            float sc[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc[g] = 0.0f;
+            if (r < n) {
+                const __half* krow = reinterpret_cast<const __half*>(kbase + r * Lay::kRow) + h * HD;
+#pragma unroll 4
+                for (int dd = 0; dd < HD; dd += 8) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(krow + dd);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                    float kf[8];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(h2[j]);
+                        kf[2 * j] = f.x;
+                        kf[2 * j + 1] = f.y;
+                    }
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) sc[g] = fmaf(qs[g][h * HD + dd + j], kf[j], sc[g]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 16);
+            if (lane < 16)
+#pragma unroll
+                for (int g = 0; g < G; ++g) ps[r][g] = r < n ? sc[g] : -INFINITY;
+        }
+        __syncthreads();
+        // online softmax bookkeeping: warp w keeps heads w, w + 4, ...
+        for (int g = warp; g < G; g += kAttThreads / 32) {
+            const float s0 = ps[lane][g], s1 = ps[lane + 32][g];
+            const float mo = m_s[g];
+            const float mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
+            const float c = mo == -INFINITY ? 0.0f : expf(mo - mn);
+            const float p0 = lane < n ? expf(s0 - mn) : 0.0f;
+            const float p1 = lane + 32 < n ? expf(s1 - mn) : 0.0f;
+            ps[lane][g] = p0;
+            ps[lane + 32][g] = p1;
+            const float sum = warp_sum(p0 + p1);
+            if (lane == 0) {
+                l_s[g] = l_s[g] * c + sum;
+                m_s[g] = mn;
+                corr_s[g] = c;
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && s + kAttStages < nsteps) mbar_expect_tx(&bars[st], step_bytes(s + kAttStages));
+        // phase 2: warp w takes keys 16w .. 16w + 15, lanes the head dims
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float c = corr_s[g];
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[g][j] *= c;
+        }
+#pragma unroll 4
+        for (int u = 0; u < 16; ++u) {
+            const int r = warp * 16 + u;
+            if (r >= n) continue;  // uniform across the warp
+            const __half* vrow = reinterpret_cast<const __half*>(vbase + r * Lay::vRow) + lane * DPL;
+            float vf[DPL];
+#pragma unroll
+            for (int j = 0; j < DPL; j += 2) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vrow + j));
+                vf[j] = f.x;
+                vf[j + 1] = f.y;
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float p = ps[r][g];
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) acc[g][j] = fmaf(p, vf[j], acc[g][j]);
+            }
+        }
+        __syncthreads();  // stage st is free again
+        if (s + kAttStages < nsteps) issue(s + kAttStages, 0);
+    }
+    if (failed) {
+        // let the copies still in flight land before the CTA exits
+        for (int s2 = s; s2 < nsteps && s2 < s + kAttStages; ++s2)
+            mbar_wait_bounded(&bars[s2 % kAttStages], (uint32_t)((s2 / kAttStages) & 1));
+        if (tid == 0) atomicExch(a.err, 3);
+        return;
+    }
+    // merge the 4 warps (the ring is idle now)
+    float* wacc = reinterpret_cast<float*>(att_smem);  // [4][G][D]
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) wacc[(warp * G + g) * D + lane * DPL + j] = acc[g][j];
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kAttThreads) {
+        const int g = i / D, dd = i - g * D;
+        const float o = ((wacc[(0 * G + g) * D + dd] + wacc[(1 * G + g) * D + dd]) + wacc[(2 * G + g) * D + dd]) +
+                        wacc[(3 * G + g) * D + dd];
+        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+        if (a.nsplit == 1) {
+            a.out[hb * D + dd] = o * (1.0f / l_s[g]);
+        } else {
+            a.part_acc[(hb * a.nsplit + split) * D + dd] = o;
+            if (dd == 0) {
+                a.part_m[hb * a.nsplit + split] = m_s[g];
+                a.part_l[hb * a.nsplit + split] = l_s[g];
+            }
+        }
+    }
+    if (a.nsplit == 1) return;
+    __syncthreads();  // every partial store precedes thread 0's release
+    if (tid == 0) flag_s = atomic_add_acq_rel_gpu(&a.counters[bk], 1) == a.nsplit - 1;
+    __syncthreads();
+    if (!flag_s) return;
+    // the last CTA of (b, kvh): split weights exp(m_s - M), then sums in split order
+    const int ns = a.nsplit;
+    float* wts = reinterpret_cast<float*>(att_smem) + 4 * G * D;  // [G][ns]
+    float* inv_l = wts + G * ns;                                   // [G]
+    for (int g = warp; g < G; g += kAttThreads / 32) {
+        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hb * ns + s2]));
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int s2 = lane; s2 < ns; s2 += 32) {
+            const float mm = __ldcg(&a.part_m[hb * ns + s2]);
+            const float w = mm == -INFINITY ? 0.0f : expf(mm - M);
+            wts[g * ns + s2] = w;
+            L += __ldcg(&a.part_l[hb * ns + s2]) * w;
+        }
+        L = warp_sum(L);
+        if (lane == 0) inv_l[g] = 1.0f / L;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kAttThreads) {
+        const int g = i / D, dd = i - g * D;
+        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+        const float* pa = a.part_acc + hb * ns * D + dd;
+        float o = 0.0f;
+        int s2 = 0;
+        for (; s2 + 8 <= ns; s2 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(pa + (int64_t)(s2 + u) * D);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) o = fmaf(v[u], wts[g * ns + s2 + u], o);
+        }
+        for (; s2 < ns; ++s2) o = fmaf(__ldcg(pa + (int64_t)s2 * D), wts[g * ns + s2], o);
+        a.out[hb * D + dd] = o * inv_l[g];
+    }
+    if (tid == 0) a.counters[bk] = 0;
+}
+
+template <int D, int G>
+void launch_decode_bulk_t(const DecodeAttnArgs& a, cudaStream_t s, bool pdl) {
+    auto kern = decode_attn_bulk_kernel<D, G>;
+    BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AttLayout<D>::smem));
+    dim3 grid((unsigned)(a.batch * a.kv_heads), (unsigned)a.nsplit);
+    launch_kernel(kern, grid, dim3(kAttThreads), AttLayout<D>::smem, s, pdl, a);
+    BC_LAUNCHED("decode_attn_bulk_kernel");
+}
+
 template <int D, int G>
 void launch_decode_t(const DecodeAttnArgs& a, cudaStream_t s, bool pdl) {
     dim3 grid((unsigned)(a.batch * a.kv_heads), (unsigned)a.nsplit);
@@ -306,9 +565,34 @@ bool decode_attention_supported(int head_dim, int group) {
     return (head_dim == 64 || head_dim == 128) && (group == 1 || group == 2 || group == 4 || group == 8);
 }
 
+int decode_bulk_splits(int batch, int kv_heads, int sm_count) {
+    const int64_t per = std::max<int64_t>(1, (int64_t)batch * kv_heads);
+    return (int)std::max<int64_t>(1, std::min<int64_t>(kMaxBulkSplits, sm_count / per));
+}
+
+size_t decode_bulk_scratch_floats(int max_batch, int heads, int kv_heads, int d, int sm_count) {
+    const int64_t g = heads / std::max(1, kv_heads);
+    const int64_t units = std::max<int64_t>((int64_t)sm_count, (int64_t)max_batch * kv_heads) +
+                          (int64_t)max_batch * kv_heads;  // + one split of slack per (sequence, KV head)
+    return (size_t)(g * units * (d + 2));
+}
+
 void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s, bool pdl) {
     const int G = a.heads / a.kv_heads;
     if (!decode_attention_supported(a.d, G)) fail(BEACON_CUDA_ERR_SHAPE_MISMATCH, "decode attention: unsupported head shape");
+    if (a.kv_f16 && a.counters && a.err) {
+        if (a.nsplit < 1 || a.nsplit > kMaxBulkSplits) invalid("decode attention: bad split count");
+        if (a.d == 128) {
+            if (G == 8) return launch_decode_bulk_t<128, 8>(a, s, pdl);
+            if (G == 4) return launch_decode_bulk_t<128, 4>(a, s, pdl);
+            if (G == 2) return launch_decode_bulk_t<128, 2>(a, s, pdl);
+            return launch_decode_bulk_t<128, 1>(a, s, pdl);
+        }
+        if (G == 8) return launch_decode_bulk_t<64, 8>(a, s, pdl);
+        if (G == 4) return launch_decode_bulk_t<64, 4>(a, s, pdl);
+        if (G == 2) return launch_decode_bulk_t<64, 2>(a, s, pdl);
+        return launch_decode_bulk_t<64, 1>(a, s, pdl);
+    }
     if (a.nsplit < 1 || a.nsplit > kMaxDecodeSplits) invalid("decode attention: bad split count");
     if (a.d == 128) {
         if (G == 8) launch_decode_t<128, 8>(a, s, pdl);

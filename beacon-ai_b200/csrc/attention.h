@@ -47,9 +47,17 @@ struct DecodeAttnArgs {
     float* part_m;
     float* part_l;
     float* out;
+    int* counters;  // [batch * kv_heads] arrival counters, zero at rest (f16 caches)
+    int* err;       // set to 3 when a bounded wait gives up (f16 caches)
 };
 constexpr int kMaxDecodeSplits = 64;
+constexpr int kMaxBulkSplits = 256;
 int plan_decode_splits(int batch, int kv_heads, int kv_len, int sm_count, int max_splits);
+// f16 caches: one CTA per (sequence, KV head, split), splits = SMs / (batch *
+// kv_heads) (at least 1), so partials need heads/kv_heads * max(SMs, batch *
+// kv_heads) * (d + 2) floats and the counters batch * kv_heads ints.
+int decode_bulk_splits(int batch, int kv_heads, int sm_count);
+size_t decode_bulk_scratch_floats(int max_batch, int heads, int kv_heads, int d, int sm_count);
 bool decode_attention_supported(int head_dim, int group);
 void launch_decode_attention(DecodeAttnArgs a, cudaStream_t s, bool pdl = false);
 

@@ -213,25 +213,26 @@ __device__ __forceinline__ void consume_q4_0(const uint4& meta, const uint4 (&q)
         for (int c = 0; c < 8; ++c) {
             const float d = half_at(meta, c);
             const uint32_t* wq = &q[c].x;
-            uint32_t lo[4], hi[4];
+            uint32_t lo[4], hi[4];  // high nibbles in place (16 x value), see consume_q4_k
 #pragma unroll
             for (int wd = 0; wd < 4; ++wd) {
                 lo[wd] = wq[wd] & 0x0F0F0F0Fu;
-                hi[wd] = (wq[wd] >> 4) & 0x0F0F0F0Fu;
+                hi[wd] = wq[wd] & 0xF0F0F0F0u;
             }
             const int blk = tile * 8 + c;
 #pragma unroll
             for (int b = 0; b < B; ++b) {
                 const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)b * span + blk * 32);
-                int ai = 0;
+                int al = 0, ah = 0;
 #pragma unroll
                 for (int wd = 0; wd < 4; ++wd) {
                     int4 X = xp[wd];
-                    ai = dp2a_lo_u8(X.x, lo[wd], ai);
-                    ai = dp2a_hi_u8(X.y, lo[wd], ai);
-                    ai = dp2a_lo_u8(X.z, hi[wd], ai);
-                    ai = dp2a_hi_u8(X.w, hi[wd], ai);
+                    al = dp2a_lo_u8(X.x, lo[wd], al);
+                    ah = dp2a_lo_u8(X.z, hi[wd], ah);
+                    al = dp2a_hi_u8(X.y, lo[wd], al);
+                    ah = dp2a_hi_u8(X.w, hi[wd], ah);
                 }
+                const int ai = al + (ah >> 4);
                 const int bi = b * nblk + blk;
                 acc[b] = fmaf(d * sx[bi], (float)(ai - 8 * sq[bi]), acc[b]);
             }
@@ -272,20 +273,21 @@ __device__ __forceinline__ void consume_q8_0(const uint4& meta, const uint4 (&q)
 #pragma unroll
             for (int b = 0; b < B; ++b) {
                 const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)b * span + blk * 32);
-                int ai = 0;
+                int a2[2] = {0, 0};
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const uint32_t* wq = &q[2 * bl + h].x;
                     int4 X = xp[2 * h], Y = xp[2 * h + 1];
-                    ai = dp2a_lo_s8(X.x, wq[0], ai);
-                    ai = dp2a_hi_s8(X.y, wq[0], ai);
-                    ai = dp2a_lo_s8(X.z, wq[1], ai);
-                    ai = dp2a_hi_s8(X.w, wq[1], ai);
-                    ai = dp2a_lo_s8(Y.x, wq[2], ai);
-                    ai = dp2a_hi_s8(Y.y, wq[2], ai);
-                    ai = dp2a_lo_s8(Y.z, wq[3], ai);
-                    ai = dp2a_hi_s8(Y.w, wq[3], ai);
+                    a2[h] = dp2a_lo_s8(X.x, wq[0], a2[h]);
+                    a2[h] = dp2a_hi_s8(X.y, wq[0], a2[h]);
+                    a2[h] = dp2a_lo_s8(X.z, wq[1], a2[h]);
+                    a2[h] = dp2a_hi_s8(X.w, wq[1], a2[h]);
+                    a2[h] = dp2a_lo_s8(Y.x, wq[2], a2[h]);
+                    a2[h] = dp2a_hi_s8(Y.y, wq[2], a2[h]);
+                    a2[h] = dp2a_lo_s8(Y.z, wq[3], a2[h]);
+                    a2[h] = dp2a_hi_s8(Y.w, wq[3], a2[h]);
                 }
+                const int ai = a2[0] + a2[1];
                 acc[b] = fmaf(d * sx[b * nblk + blk], (float)ai, acc[b]);
             }
         }
@@ -353,6 +355,8 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
         const int* sq = reinterpret_cast<const int*>(sx + B * nblk);
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {
+            // low nibbles as bytes; high nibbles kept in place (16 x value): the
+            // integer sums below are exact, so >> 4 recovers the true sum
             uint32_t lo[2][4], hi[2][4];
 #pragma unroll
             for (int h = 0; h < 2; ++h)
@@ -360,7 +364,7 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
                 for (int wd = 0; wd < 4; ++wd) {
                     uint32_t w = (&q[2 * pr + h].x)[wd];
                     lo[h][wd] = w & 0x0F0F0F0Fu;
-                    hi[h][wd] = (w >> 4) & 0x0F0F0F0Fu;
+                    hi[h][wd] = w & 0xF0F0F0F0u;
                 }
             const float dl = d * (float)sc[2 * pr], dh = d * (float)sc[2 * pr + 1];
             const float ml = dmin * (float)mn[2 * pr], mh = dmin * (float)mn[2 * pr + 1];
@@ -369,31 +373,32 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
             for (int b = 0; b < B; ++b) {
                 const int4* xl = reinterpret_cast<const int4*>(xq + (size_t)b * span + jl * 32);
                 const int4* xh = reinterpret_cast<const int4*>(xq + (size_t)b * span + jh * 32);
-                int al = 0, ah = 0;
+                int al[2] = {0, 0}, ah[2] = {0, 0};
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     int4 L0 = xl[2 * h], L1 = xl[2 * h + 1];
                     int4 H0 = xh[2 * h], H1 = xh[2 * h + 1];
-                    al = dp2a_lo_u8(L0.x, lo[h][0], al);
-                    al = dp2a_hi_u8(L0.y, lo[h][0], al);
-                    al = dp2a_lo_u8(L0.z, lo[h][1], al);
-                    al = dp2a_hi_u8(L0.w, lo[h][1], al);
-                    al = dp2a_lo_u8(L1.x, lo[h][2], al);
-                    al = dp2a_hi_u8(L1.y, lo[h][2], al);
-                    al = dp2a_lo_u8(L1.z, lo[h][3], al);
-                    al = dp2a_hi_u8(L1.w, lo[h][3], al);
-                    ah = dp2a_lo_u8(H0.x, hi[h][0], ah);
-                    ah = dp2a_hi_u8(H0.y, hi[h][0], ah);
-                    ah = dp2a_lo_u8(H0.z, hi[h][1], ah);
-                    ah = dp2a_hi_u8(H0.w, hi[h][1], ah);
-                    ah = dp2a_lo_u8(H1.x, hi[h][2], ah);
-                    ah = dp2a_hi_u8(H1.y, hi[h][2], ah);
-                    ah = dp2a_lo_u8(H1.z, hi[h][3], ah);
-                    ah = dp2a_hi_u8(H1.w, hi[h][3], ah);
+                    al[h] = dp2a_lo_u8(L0.x, lo[h][0], al[h]);
+                    ah[h] = dp2a_lo_u8(H0.x, hi[h][0], ah[h]);
+                    al[h] = dp2a_hi_u8(L0.y, lo[h][0], al[h]);
+                    ah[h] = dp2a_hi_u8(H0.y, hi[h][0], ah[h]);
+                    al[h] = dp2a_lo_u8(L0.z, lo[h][1], al[h]);
+                    ah[h] = dp2a_lo_u8(H0.z, hi[h][1], ah[h]);
+                    al[h] = dp2a_hi_u8(L0.w, lo[h][1], al[h]);
+                    ah[h] = dp2a_hi_u8(H0.w, hi[h][1], ah[h]);
+                    al[h] = dp2a_lo_u8(L1.x, lo[h][2], al[h]);
+                    ah[h] = dp2a_lo_u8(H1.x, hi[h][2], ah[h]);
+                    al[h] = dp2a_hi_u8(L1.y, lo[h][2], al[h]);
+                    ah[h] = dp2a_hi_u8(H1.y, hi[h][2], ah[h]);
+                    al[h] = dp2a_lo_u8(L1.z, lo[h][3], al[h]);
+                    ah[h] = dp2a_lo_u8(H1.z, hi[h][3], ah[h]);
+                    al[h] = dp2a_hi_u8(L1.w, lo[h][3], al[h]);
+                    ah[h] = dp2a_hi_u8(H1.w, hi[h][3], ah[h]);
                 }
+                const int sl = al[0] + al[1], sh = (ah[0] + ah[1]) >> 4;
                 const int bl = b * nblk + jl, bh = b * nblk + jh;
-                float v = sx[bl] * (dl * (float)al - ml * (float)sq[bl]) +
-                          sx[bh] * (dh * (float)ah - mh * (float)sq[bh]);
+                float v = sx[bl] * (dl * (float)sl - ml * (float)sq[bl]) +
+                          sx[bh] * (dh * (float)sh - mh * (float)sq[bh]);
                 acc[b] += v;
             }
         }

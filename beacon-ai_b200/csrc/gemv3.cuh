@@ -26,7 +26,6 @@
 namespace bc {
 
 constexpr int kG3Warps = 8;
-constexpr long long kG3WaitLimit = 1LL << 31;
 
 struct Gemv3Params {
     GemvParams p;         // w, n, n_pad, x, x_f16, x_ld, k, batch, y, y_ld, res, res_ld, rtz, norm_w
@@ -40,173 +39,256 @@ struct Gemv3Params {
     int* err;             // set to 1 when a wait gives up
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
+// Staging of the activations. Thread t of pass i covers columns
+// c = (256 i + t) * 4 .. c + 3, so the 8 lanes t = 8m .. 8m+7 of a warp hold
+// one 32-column block and reduce its absmax and code sum with shuffles. Up to
+// kStageRegPasses passes (8192 columns) stay in registers, so the fused
+// RMSNorm reads each activation once; the norm weights are fetched before the
+// kernel waits on its predecessor (weights are never written).
+constexpr int kStageRegPasses = 8;
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait; false if the limit was reached.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > kG3WaitLimit) return false;
-    return true;
-}
-
-// 32 consecutive activations of row b starting at column c (zero past k),
-// RMSNorm-scaled when a norm weight is given.
-template <int B>
-__device__ __forceinline__ void load_x32(const GemvParams& p, bool vec, int b, int64_t c, const float* inv,
-                                         float (&v)[32]) {
-    if (vec && b < p.batch && c + 31 < p.k) {
-        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + b * p.x_ld + c);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 f = src[q];
-            v[4 * q] = f.x;
-            v[4 * q + 1] = f.y;
-            v[4 * q + 2] = f.z;
-            v[4 * q + 3] = f.w;
+__device__ __forceinline__ float4 load_x4(const GemvParams& p, bool vec, int b, int64_t c) {
+    if (b >= p.batch || c >= p.k) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (vec && c + 3 < p.k) {
+        if (p.x_f16) {
+            const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.x) + b * p.x_ld + c);
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            return make_float4(lo.x, lo.y, hi.x, hi.y);
         }
-    } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = load_x(p, b, c + e);
+        return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + b * p.x_ld + c);
     }
-    if (p.norm_w && b < p.batch) {
-        const float r = inv[b];
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-            if (c + e < p.k) v[e] = v[e] * r * p.norm_w[c + e];  // (x * inv_rms) * w, ops.rs:91
-    }
+    return make_float4(load_x(p, b, c), load_x(p, b, c + 1), load_x(p, b, c + 2), load_x(p, b, c + 3));
 }
 
-// Staging of all K columns (FAST: int16 codes + scale + sum per 32 with the
-// format's element order; F32: floats). Same layout as gemv.cuh's stage_x
-// with span = kspan. All threads of the CTA take part.
-template <int FMT, int MODE, int B>
-__device__ __forceinline__ void stage_x_full(const GemvParams& p, uint8_t* xs, int kspan) {
-    __shared__ float part[kG3Warps][B];
-    __shared__ float inv[B];
-    const bool vec = !p.x_f16 && (p.x_ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
-    if (p.norm_w) {
-        // sum of squares per row in a fixed order: lanes, then warps
-        float ss[B];
+// norm weights of columns c .. c+3 (zero past k)
+__device__ __forceinline__ float4 load_norm4(const GemvParams& p, bool vec, int64_t c) {
+    if (vec && c + 3 < p.k) return __ldg(reinterpret_cast<const float4*>(p.norm_w + c));
+    float4 w;
+    w.x = c < p.k ? p.norm_w[c] : 0.0f;
+    w.y = c + 1 < p.k ? p.norm_w[c + 1] : 0.0f;
+    w.z = c + 2 < p.k ? p.norm_w[c + 2] : 0.0f;
+    w.w = c + 3 < p.k ? p.norm_w[c + 3] : 0.0f;
+    return w;
+}
+
+__device__ __forceinline__ int stage_passes(int kspan) { return (kspan + 1023) / 1024; }
+
+__device__ __forceinline__ bool norm_vec_ok(const GemvParams& p) {
+    return (reinterpret_cast<uintptr_t>(p.norm_w) & 15) == 0;
+}
+
+// Norm weights of the register-resident passes; called before the wait on
+// the previous kernel.
+__device__ __forceinline__ void prefetch_norm(const GemvParams& p, int kspan, float4 (&nw)[kStageRegPasses]) {
 #pragma unroll
-        for (int b = 0; b < B; ++b) ss[b] = 0.0f;
-        for (int64_t c = (int64_t)threadIdx.x * 4; c < p.k; c += (int64_t)blockDim.x * 4) {
+    for (int i = 0; i < kStageRegPasses; ++i) nw[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const int passes = stage_passes(kspan);
+    if (!p.norm_w || passes > kStageRegPasses) return;
+    const bool vec = norm_vec_ok(p);
 #pragma unroll
-            for (int b = 0; b < B; ++b) {
-                if (b >= p.batch) break;
-                float4 f;
-                if (vec && c + 3 < p.k) {
-                    f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + b * p.x_ld + c);
-                } else {
-                    f.x = load_x(p, b, c);
-                    f.y = load_x(p, b, c + 1);
-                    f.z = load_x(p, b, c + 2);
-                    f.w = load_x(p, b, c + 3);
-                }
-                ss[b] = fmaf(f.x, f.x, ss[b]);
-                ss[b] = fmaf(f.y, f.y, ss[b]);
-                ss[b] = fmaf(f.z, f.z, ss[b]);
-                ss[b] = fmaf(f.w, f.w, ss[b]);
-            }
-        }
-        const int warp = threadIdx.x >> 5;
-#pragma unroll
-        for (int b = 0; b < B; ++b) {
-            const float w = warp_sum(ss[b]);
-            if ((threadIdx.x & 31) == 0) part[warp][b] = w;
-        }
-        __syncthreads();
-        if (threadIdx.x < B) {
-            float t = 0.0f;
-            for (int w = 0; w < kG3Warps; ++w) t += part[w][threadIdx.x];
-            inv[threadIdx.x] = 1.0f / sqrtf(t / (float)p.k + p.norm_eps);
-        }
-        __syncthreads();
-    }
+    for (int i = 0; i < kStageRegPasses; ++i)
+        if (i < passes) nw[i] = load_norm4(p, vec, (int64_t)(i * 256 + threadIdx.x) * 4);
+}
+
+__device__ __forceinline__ uint32_t pack_i16x2(int lo, int hi) { return (uint32_t)(lo & 0xFFFF) | ((uint32_t)hi << 16); }
+
+// Quantise NP passes of 4 activations per lane to int16 codes with one scale
+// per 32-column block (scale ~ absmax / 32767, codes = round(v * 32767 /
+// absmax) with a correctly rounded reciprocal, clamped to +-32767); Q4_0 takes
+// each 8-group in the order e0 e2 e4 e6 e1 e3 e5 e7 to match its nibble pairs.
+// The passes are processed stage by stage (all absmax shuffles, then all
+// codes, ...) so they overlap. Every lane of the warp calls this; only
+// columns c < kspan are stored. v: activations (already normalised), pass i
+// covers columns (p0 + i) * 1024 + 4 * threadIdx.x.
+template <int FMT, int MODE, int NP>
+__device__ __forceinline__ void store_passes(const float4 (&v)[NP], int p0, int kspan, uint8_t* xs, int b, int B,
+                                             int nblk) {
+    const int tid = threadIdx.x;
     if (MODE == MODE_F32) {
-        float* o = reinterpret_cast<float*>(xs);
-        const int nblk = kspan / 32;
-        for (int i = threadIdx.x; i < B * nblk; i += blockDim.x) {
-            const int b = i / nblk, j = i - b * nblk;
-            float v[32];
-            load_x32<B>(p, vec, b, (int64_t)j * 32, inv, v);
-            float4* dst = reinterpret_cast<float4*>(o + (size_t)b * kspan + j * 32);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        for (int i = 0; i < NP; ++i) {
+            const int c = (p0 + i) * 1024 + 4 * tid;
+            if (c < kspan) *reinterpret_cast<float4*>(reinterpret_cast<float*>(xs) + (size_t)b * kspan + c) = v[i];
         }
         return;
     }
-    int16_t* xq = reinterpret_cast<int16_t*>(xs);
-    const int nblk = kspan / 32;
-    float* sx = reinterpret_cast<float*>(xs + (size_t)B * kspan * 2);
-    int* sq = reinterpret_cast<int*>(sx + B * nblk);
-    for (int i = threadIdx.x; i < B * nblk; i += blockDim.x) {
-        const int b = i / nblk, j = i - b * nblk;
-        float v[32];
-        load_x32<B>(p, vec, b, (int64_t)j * 32, inv, v);
-        float amax = 0.0f;
+    int16_t* xq = reinterpret_cast<int16_t*>(xs) + (size_t)b * kspan;
+    float* sx = reinterpret_cast<float*>(xs + (size_t)B * kspan * 2) + b * nblk;
+    int* sq = reinterpret_cast<int*>(reinterpret_cast<float*>(xs + (size_t)B * kspan * 2) + B * nblk) + b * nblk;
+    float am[NP];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
-        const float qi = amax > 0.0f ? __fdiv_rn(32767.0f, amax) : 0.0f;
-        int sum = 0;
-        int qv[32];
+    for (int i = 0; i < NP; ++i) am[i] = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            qv[e] = max(-32767, min(32767, __float2int_rn(__fmul_rn(v[e], qi))));
-            sum += qv[e];
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < NP; ++i) am[i] = fmaxf(am[i], __shfl_xor_sync(0xffffffffu, am[i], o));
+    int q[NP][4], sum[NP];
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+        const float qi = am[i] > 0.0f ? 32767.0f * __frcp_rn(am[i]) : 0.0f;
+        q[i][0] = max(-32767, min(32767, __float2int_rn(__fmul_rn(v[i].x, qi))));
+        q[i][1] = max(-32767, min(32767, __float2int_rn(__fmul_rn(v[i].y, qi))));
+        q[i][2] = max(-32767, min(32767, __float2int_rn(__fmul_rn(v[i].z, qi))));
+        q[i][3] = max(-32767, min(32767, __float2int_rn(__fmul_rn(v[i].w, qi))));
+        sum[i] = (q[i][0] + q[i][1]) + (q[i][2] + q[i][3]);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < NP; ++i) sum[i] += __shfl_xor_sync(0xffffffffu, sum[i], o);
+    const bool even = (tid & 1) == 0;  // Q4_0: even lanes hold e0..e3 of an 8-group, odd lanes e4..e7
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+        uint32_t lo, hi;
+        if (FMT == FMT_Q4_0) {
+            const uint32_t send = even ? pack_i16x2(q[i][1], q[i][3]) : pack_i16x2(q[i][0], q[i][2]);
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            lo = even ? pack_i16x2(q[i][0], q[i][2]) : recv;
+            hi = even ? recv : pack_i16x2(q[i][1], q[i][3]);
+        } else {
+            lo = pack_i16x2(q[i][0], q[i][1]);
+            hi = pack_i16x2(q[i][2], q[i][3]);
         }
-        uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-            int a0, a1;
-            if (FMT == FMT_Q4_0) {  // 8-groups as e0 e2 e4 e6 e1 e3 e5 e7, matching the nibble pairs
-                const int grp = e & ~7, s0 = e & 7, s1 = s0 + 1;
-                a0 = qv[grp + (s0 < 4 ? 2 * s0 : 2 * (s0 - 4) + 1)];
-                a1 = qv[grp + (s1 < 4 ? 2 * s1 : 2 * (s1 - 4) + 1)];
-            } else {
-                a0 = qv[e];
-                a1 = qv[e + 1];
+        const int c = (p0 + i) * 1024 + 4 * tid;
+        if (c < kspan) {
+            *reinterpret_cast<uint2*>(xq + c) = make_uint2(lo, hi);
+            if ((tid & 7) == 0) {
+                sx[c >> 5] = am[i] * (1.0f / 32767.0f);
+                sq[c >> 5] = sum[i];
             }
-            packed[e / 2] = (uint32_t)(a0 & 0xFFFF) | ((uint32_t)a1 << 16);
         }
-        uint4* dst = reinterpret_cast<uint4*>(xq + (size_t)b * kspan + j * 32);
+    }
+}
+
+// One chunk of NP passes loaded from global (rows beyond the register-held
+// size), normalised with inv and the norm weights when given, then stored.
+template <int FMT, int MODE, int NP>
+__device__ __forceinline__ void stage_chunk(const GemvParams& p, bool vec, bool wvec, int b, int p0, float inv,
+                                            int kspan, uint8_t* xs, int B, int nblk) {
+    float4 v[NP];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-        sx[b * nblk + j] = amax > 0.0f ? __fdiv_rn(amax, 32767.0f) : 0.0f;
-        sq[b * nblk + j] = sum;
+    for (int i = 0; i < NP; ++i) v[i] = load_x4(p, vec, b, (int64_t)((p0 + i) * 256 + threadIdx.x) * 4);
+    if (p.norm_w) {
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+            const float4 w = load_norm4(p, wvec, (int64_t)((p0 + i) * 256 + threadIdx.x) * 4);
+            v[i].x = v[i].x * inv * w.x;  // (x * inv_rms) * w, ops.rs:91
+            v[i].y = v[i].y * inv * w.y;
+            v[i].z = v[i].z * inv * w.z;
+            v[i].w = v[i].w * inv * w.w;
+        }
+    }
+    store_passes<FMT, MODE, NP>(v, p0, kspan, xs, b, B, nblk);
+}
+
+// Register-held rows (passes <= 8): NP = passes rounded up to a power of two.
+template <int FMT, int MODE, int NP>
+__device__ __forceinline__ void stage_held(const GemvParams& p, const float4 (&xr)[kStageRegPasses],
+                                           const float4 (&nwr)[kStageRegPasses], float inv, int kspan, uint8_t* xs,
+                                           int b, int B, int nblk) {
+    float4 v[NP];
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+        v[i] = xr[i];
+        if (p.norm_w) {
+            v[i].x = v[i].x * inv * nwr[i].x;  // (x * inv_rms) * w, ops.rs:91
+            v[i].y = v[i].y * inv * nwr[i].y;
+            v[i].z = v[i].z * inv * nwr[i].z;
+            v[i].w = v[i].w * inv * nwr[i].w;
+        }
+    }
+    store_passes<FMT, MODE, NP>(v, 0, kspan, xs, b, B, nblk);
+}
+
+// Staging of all K columns (FAST: int16 codes + scale + code sum per 32;
+// F32: floats), rows b >= batch and columns >= k as zeros, with the optional
+// RMSNorm (x * inv_rms) * w of ops.rs:77-93. All threads of the CTA take part.
+template <int FMT, int MODE, int B>
+__device__ __forceinline__ void stage_x_full(const GemvParams& p, uint8_t* xs, int kspan,
+                                             const float4 (&nwr)[kStageRegPasses]) {
+    __shared__ float part[B][kG3Warps];
+    constexpr int R = kStageRegPasses;
+    const bool vec = (p.x_ld % 4 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(p.x) & (p.x_f16 ? 7 : 15)) == 0);
+    const bool wvec = p.norm_w && norm_vec_ok(p);
+    const int passes = stage_passes(kspan);
+    const bool held = passes <= R;
+    const int nblk = kspan / 32;
+    const int warp = threadIdx.x >> 5;
+#pragma unroll 1
+    for (int b = 0; b < B; ++b) {
+        float4 xr[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) xr[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (held) {
+#pragma unroll
+            for (int i = 0; i < R; ++i)
+                if (i < passes) xr[i] = load_x4(p, vec, b, (int64_t)(i * 256 + threadIdx.x) * 4);
+        }
+        float inv = 1.0f;
+        if (p.norm_w) {
+            // sum of squares in a fixed order: passes per lane, lanes, warps
+            float ss = 0.0f;
+            if (held) {
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    ss = fmaf(xr[i].x, xr[i].x, ss);
+                    ss = fmaf(xr[i].y, xr[i].y, ss);
+                    ss = fmaf(xr[i].z, xr[i].z, ss);
+                    ss = fmaf(xr[i].w, xr[i].w, ss);
+                }
+            } else {
+                for (int p0 = 0; p0 < passes; p0 += R) {
+                    float4 t[R];
+#pragma unroll
+                    for (int i = 0; i < R; ++i)
+                        t[i] = p0 + i < passes ? load_x4(p, vec, b, (int64_t)((p0 + i) * 256 + threadIdx.x) * 4)
+                                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        ss = fmaf(t[i].x, t[i].x, ss);
+                        ss = fmaf(t[i].y, t[i].y, ss);
+                        ss = fmaf(t[i].z, t[i].z, ss);
+                        ss = fmaf(t[i].w, t[i].w, ss);
+                    }
+                }
+            }
+            ss = warp_sum(ss);
+            if ((threadIdx.x & 31) == 0) part[b][warp] = ss;
+            __syncthreads();
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kG3Warps; ++w) tot += part[b][w];
+            inv = 1.0f / sqrtf(tot / (float)p.k + p.norm_eps);
+        }
+        if (held) {
+            if (passes <= 1)
+                stage_held<FMT, MODE, 1>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+            else if (passes <= 2)
+                stage_held<FMT, MODE, 2>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+            else if (passes <= 4)
+                stage_held<FMT, MODE, 4>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+            else
+                stage_held<FMT, MODE, 8>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+        } else {
+            int p0 = 0;
+            for (; p0 + 8 <= passes; p0 += 8) stage_chunk<FMT, MODE, 8>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+            if (p0 + 4 <= passes) {
+                stage_chunk<FMT, MODE, 4>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+                p0 += 4;
+            }
+            if (p0 + 2 <= passes) {
+                stage_chunk<FMT, MODE, 2>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+                p0 += 2;
+            }
+            if (p0 < passes) stage_chunk<FMT, MODE, 1>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+        }
     }
 }
 
 template <int FMT, int MODE, int B>
-__global__ void __launch_bounds__(kG3Warps * 32, 1) qgemv3_kernel(const Gemv3Params a, const int epi) {
+__global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel(const Gemv3Params a, const int epi) {
     extern __shared__ __align__(128) uint8_t g3_smem[];
     uint8_t* smem = g3_smem;
     constexpr int CH = Fmt<FMT>::CH;
@@ -235,9 +317,11 @@ __global__ void __launch_bounds__(kG3Warps * 32, 1) qgemv3_kernel(const Gemv3Par
             mbar_expect_tx(&mybar[i], (uint32_t)tb);
             bulk_g2s(myring + (size_t)i * tb, p.w + (t_begin + i) * tb, (uint32_t)tb, &mybar[i]);
         }
+    float4 nwr[kStageRegPasses];
+    prefetch_norm(p, a.kspan, nwr);
     pdl_trigger();
     pdl_wait();
-    stage_x_full<FMT, MODE, B>(p, xs, a.kspan);
+    stage_x_full<FMT, MODE, B>(p, xs, a.kspan, nwr);
     __syncthreads();
 
     float acc[B];
@@ -245,6 +329,11 @@ __global__ void __launch_bounds__(kG3Warps * 32, 1) qgemv3_kernel(const Gemv3Par
     for (int b = 0; b < B; ++b) acc[b] = 0.0f;
     const bool rtz = p.rtz != 0;
     bool ok = true;
+    // 32-bit tile arithmetic (the host keeps total_tiles * total_warps < 2^32)
+    const uint32_t T = (uint32_t)a.total_tiles, W = (uint32_t)a.total_warps, KT = (uint32_t)a.ktiles;
+    const uint32_t tb0 = (uint32_t)t_begin, te0 = (uint32_t)t_end;
+    uint32_t g = tb0 / KT;        // row group of the current tile
+    uint32_t t = tb0 - g * KT;    // its k-tile
     int i = 0;
     for (; i < n; ++i) {
         const int st = i % S;
@@ -263,44 +352,56 @@ __global__ void __launch_bounds__(kG3Warps * 32, 1) qgemv3_kernel(const Gemv3Par
             mbar_expect_tx(&mybar[st], (uint32_t)tb);
             bulk_g2s(myring + (size_t)st * tb, p.w + (t_begin + i + S) * tb, (uint32_t)tb, &mybar[st]);
         }
-        const int64_t tl = t_begin + i;
-        const int64_t g = tl / a.ktiles;
-        const int t = (int)(tl - g * a.ktiles);
         if (FMT == FMT_Q4_0)
-            consume_q4_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), xs, a.kspan, t, acc, rtz);
+            consume_q4_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), xs, a.kspan, (int)t, acc, rtz);
         else if (FMT == FMT_Q8_0)
-            consume_q8_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[16]>(q), xs, a.kspan, t, acc, rtz);
+            consume_q8_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[16]>(q), xs, a.kspan, (int)t, acc, rtz);
         else
-            consume_q4_k<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), xs, a.kspan, t, acc, rtz);
+            consume_q4_k<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), xs, a.kspan, (int)t, acc, rtz);
         // end of a row group (or of this warp's range): finish it
-        if (t == a.ktiles - 1 || i == n - 1) {
-            const int64_t g0 = g * a.ktiles, g1 = g0 + a.ktiles;
-            if (g0 >= t_begin && g1 <= t_end) {
+        if (t == KT - 1 || i == n - 1) {
+            const uint32_t g0 = g * KT, g1 = g0 + KT;
+            if (g0 >= tb0 && g1 <= te0) {
                 gemv_store<B>(p, epi, g, lane, acc);
             } else {
                 // contributors to group g: warps whose ranges meet [g0, g1)
-                const int64_t wf = ((g0 + 1) * a.total_warps - 1) / a.total_tiles;
-                const int64_t wl = (g1 * a.total_warps - 1) / a.total_tiles;
-                const int slot = (t_begin >= g0) ? 0 : 1;  // 0: g is the first group of my range
+                const uint32_t wf = ((g0 + 1) * W - 1) / T;
+                const uint32_t wl = (g1 * W - 1) / T;
+                const int slot = (tb0 >= g0) ? 0 : 1;  // 0: g is the first group of my range
                 float* mine = a.slots + ((gw * 2 + slot) * B) * 32;
 #pragma unroll
-                for (int b = 0; b < B; ++b) mine[b * 32 + lane] = acc[b];
-                __threadfence();
+                for (int b = 0; b < B; ++b) __stcg(&mine[b * 32 + lane], acc[b]);
+                // __syncwarp orders the lanes' stores before lane 0's release;
+                // the last arriver's acquire makes every contributor's visible
                 __syncwarp();
                 int last = 0;
-                if (lane == 0) last = atomicAdd(&a.counters[g], 1) == (int)(wl - wf);
+                if (lane == 0) last = atomic_add_acq_rel_gpu(&a.counters[g], 1) == (int)(wl - wf);
                 last = __shfl_sync(0xffffffffu, last, 0);
+                __syncwarp();
                 if (last) {
-                    __threadfence();
+                    constexpr int U = B >= 8 ? 1 : 8 / B;  // contributor slots loaded together
                     float v[B];
 #pragma unroll
                     for (int b = 0; b < B; ++b) v[b] = 0.0f;
-                    for (int64_t w2 = wf; w2 <= wl; ++w2) {
-                        const int64_t s2 = w2 * a.total_tiles / a.total_warps;
-                        const int sl = (s2 >= g0) ? 0 : 1;  // g is w2's first group iff its range starts in g
-                        const float* src = a.slots + ((w2 * 2 + sl) * B) * 32;
+                    for (uint32_t w0 = wf; w0 <= wl; w0 += U) {
+                        float part[U][B];
 #pragma unroll
-                        for (int b = 0; b < B; ++b) v[b] += __ldcg(&src[b * 32 + lane]);
+                        for (int u = 0; u < U; ++u) {
+                            const uint32_t w2 = w0 + u;
+                            if (w2 <= wl) {
+                                const uint32_t s2 = w2 * T / W;
+                                const int sl = (s2 >= g0) ? 0 : 1;  // g is w2's first group iff its range starts in g
+                                const float* src = a.slots + (((int64_t)w2 * 2 + sl) * B) * 32;
+#pragma unroll
+                                for (int b = 0; b < B; ++b) part[u][b] = __ldcg(&src[b * 32 + lane]);
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < U; ++u)
+                            if (w0 + u <= wl) {
+#pragma unroll
+                                for (int b = 0; b < B; ++b) v[b] += part[u][b];
+                            }
                     }
                     gemv_store<B>(p, epi, g, lane, v);
                     if (lane == 0) a.counters[g] = 0;
@@ -308,6 +409,10 @@ __global__ void __launch_bounds__(kG3Warps * 32, 1) qgemv3_kernel(const Gemv3Par
             }
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = 0.0f;
+        }
+        if (++t == KT) {
+            t = 0;
+            ++g;
         }
     }
     if (!ok) {

@@ -50,20 +50,29 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
 // The persistent kernel is used for batch <= 8 when at least 2 ring stages
 // per warp and the staged activations fit under the opt-in shared memory, and
 // there are at least as many tiles as warps (every warp range non-empty).
+// Batch <= 2 builds hold at most 128 registers per thread, so two CTAs fit on
+// an SM: the ring is then sized to keep a CTA under half the SM's shared
+// memory, which lets the next kernel's CTA start (and fetch its weights)
+// while this one finishes, and GEMVs with many tiles per warp run two CTAs
+// per SM for more warps in flight.
 LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
     LinearPlan pl;
     pl.v2 = plan_qgemv(ctx, L, batch, mode);
     if (batch > 8) return pl;
     pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : 8;
-    const size_t budget = 200 * 1024;
+    const size_t budget = 200 * 1024, half_sm = 110 * 1024;
     const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad);
     const size_t tb = (size_t)L.tile_bytes;
     if (xb + 256 + 2 * kG3Warps * tb > budget) return pl;
     int stages = (int)std::min<size_t>(6, (budget - xb - 256) / (kG3Warps * tb));
+    const bool pairable = pl.bpad <= 2 && xb + 256 + 2 * kG3Warps * tb <= half_sm;
+    if (pairable) stages = (int)std::min<size_t>(stages, (half_sm - xb - 256) / (kG3Warps * tb));
     const int64_t total_tiles = L.groups() * L.ktiles();
     const int sms = ctx ? ctx->sm_count : 148;
-    const int64_t nctas = std::min<int64_t>(sms, total_tiles / kG3Warps);
+    const int cps = pairable && total_tiles >= (int64_t)sms * kG3Warps * 8 ? 2 : 1;
+    const int64_t nctas = std::min<int64_t>((int64_t)sms * cps, total_tiles / kG3Warps);
     if (nctas < 1) return pl;
+    if ((uint64_t)total_tiles * (uint64_t)(nctas * kG3Warps) >= (1ull << 32)) return pl;  // 32-bit tile arithmetic
     pl.v3 = true;
     pl.stages = stages;
     pl.nctas = (int)nctas;

@@ -225,6 +225,7 @@ struct BeaconCudaModel {
     std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
     int attn_nsplit = 1;
     float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
+    int* attn_cnt = nullptr;
     std::unique_ptr<bc::DeviceBuffer> argmax_buf;
     bool pdl = true;  // programmatic dependent launch between the step's kernels
     bc::ArgmaxSummary* argmax_scratch = nullptr;
@@ -325,7 +326,9 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.kv_len = pos_imm + 1;
             a.max_kv = c.max_context;
             a.scale = scale;
-            a.nsplit = m->attn_nsplit;
+            a.nsplit = f16kv ? decode_bulk_splits(rows, m->kv_loc, m->ctx->sm_count) : m->attn_nsplit;
+            a.counters = m->attn_cnt;
+            a.err = m->err_dev;
             a.part_acc = m->pacc;
             a.part_m = m->pm;
             a.part_l = m->pl;
@@ -411,6 +414,7 @@ void check_err(BeaconCudaModel* m, cudaStream_t s) {
     if (herr) {
         BC_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), s));
         if (herr == 2) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
+        if (herr == 3) fail(BEACON_CUDA_ERR_CUDA, "decode attention: a bounded wait for the KV cache copies gave up");
         shape_err("token id out of range for the vocabulary");
     }
 }
@@ -573,11 +577,19 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
         m->err_dev = m->pos_dev + 16;
         // attention split scratch (decode)
         m->attn_nsplit = plan_decode_splits(c.max_batch, m->kv_loc, c.max_context, ctx->sm_count, 64);
-        const size_t pa = (size_t)c.max_batch * m->h_loc * m->attn_nsplit;
-        m->attn_buf = std::make_unique<DeviceBuffer>((pa * c.head_dim + 2 * pa) * 4);
+        // partial rows (head, split) of either decode kernel, then the f16
+        // kernel's arrival counters (zero at rest)
+        const size_t pa = std::max((size_t)c.max_batch * m->h_loc * m->attn_nsplit,
+                                   decode_bulk_scratch_floats((int)c.max_batch, (int)m->h_loc, (int)m->kv_loc,
+                                                              (int)c.head_dim, ctx->sm_count) /
+                                       (size_t)(c.head_dim + 2));
+        const size_t ncnt = (size_t)c.max_batch * m->kv_loc;
+        m->attn_buf = std::make_unique<DeviceBuffer>((pa * c.head_dim + 2 * pa) * 4 + ncnt * 4);
         m->pacc = static_cast<float*>(m->attn_buf->ptr);
         m->pm = m->pacc + pa * c.head_dim;
         m->pl = m->pm + pa;
+        m->attn_cnt = reinterpret_cast<int*>(m->pl + pa);
+        BC_CUDA(cudaMemset(m->attn_cnt, 0, ncnt * 4));
         const size_t na = argmax_scratch_count(m->v_loc, tp, (int)R);
         m->argmax_buf = std::make_unique<DeviceBuffer>(na * sizeof(ArgmaxSummary));
         m->argmax_scratch = static_cast<ArgmaxSummary*>(m->argmax_buf->ptr);
