@@ -271,37 +271,49 @@ __global__ void decode_attn_combine_kernel(const DecodeAttnArgs a, int d) {
 }
 
 // Decode attention over an f16 KV cache ------------------------------------------
-// One CTA (4 warps) per (sequence, KV head, split of the keys). The split's
-// key and value rows are staged in shared memory by 1-D bulk copies, 64 keys
-// per stage in a ring of up to 4 stages; every row except the decoded token's
+// One CTA (8 warps) per (sequence, KV head, split of the keys). The split's
+// key and value rows are staged in shared memory with 16-byte asynchronous
+// copies, 64 keys per stage in a ring of up to 4 stages whose completion is
+// tracked by one mbarrier per stage. Every row except the decoded token's
 // (written by the previous kernel) is requested before the kernel waits on its
-// predecessor, so the cache stream overlaps the preceding GEMV. Phase 1: each
-// key is taken by a lane pair of one warp (half the head dims each) for all G
-// query heads of the KV head; phase 2: lanes over head dims accumulate p * v,
-// with an online softmax across stages (engine.rs:415-440). The splits of a
-// (sequence, KV head) are merged in split order by the last of its CTAs to
-// finish (arrival counter), so no separate combine kernel runs.
+// predecessor, so the cache stream overlaps the preceding GEMV.
+// Scores: lane l holds head dims [l*DPL, l*DPL+DPL) of all G query heads in
+// registers; a warp takes 32/G keys at a time and a transposing butterfly
+// (31 shuffles) leaves lane l with the full dot product of (key l/G, head
+// l%G). Values: lanes over head dims, warps over keys, with an online softmax
+// across stages (engine.rs:415-440). The splits of a (sequence, KV head) are
+// merged in split order by the last of its CTAs to finish (arrival counter),
+// so no separate combine kernel runs.
 constexpr int kAttKeys = 64;
 constexpr int kAttStages = 4;
-constexpr int kAttThreads = 128;
+constexpr int kAttThreads = 256;
+constexpr int kAttWarps = kAttThreads / 32;
 
 template <int D>
 struct AttLayout {
-    static constexpr int kRow = 2 * D + 16;  // padded key row: 8 lanes' rows fall in distinct banks
-    static constexpr int vRow = 2 * D;
-    static constexpr int stage = kAttKeys * (kRow + vRow);
+    static constexpr int row = 2 * D;                      // bytes of one key or value row
+    static constexpr int stage = 2 * kAttKeys * row;       // keys, then values
+    static constexpr int chunks = 2 * kAttKeys * row / 16;  // 16-byte copies per stage
     static constexpr size_t smem = (size_t)kAttStages * stage;
 };
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// The barrier receives one arrival from this thread once all of its earlier
+// asynchronous copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 template <int D, int G>
-__global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const DecodeAttnArgs a) {
+__global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const DecodeAttnArgs a) {
     using Lay = AttLayout<D>;
-    constexpr int DPL = D / 32;  // phase 2: head dims per lane
-    constexpr int HD = D / 2;    // phase 1: head dims per lane of a pair
-    static_assert(kAttThreads == 2 * kAttKeys, "one thread per staged row");
+    constexpr int DPL = D / 32;   // head dims per lane
+    constexpr int KB = 32 / G;    // keys per score batch
+    constexpr int NB = kAttKeys / KB;  // score batches per stage
     extern __shared__ __align__(128) uint8_t att_smem[];
     __shared__ __align__(8) uint64_t bars[kAttStages];
-    __shared__ __align__(16) float qs[G][D];
     __shared__ __align__(16) float ps[kAttKeys][G];
     __shared__ float corr_s[G], m_s[G], l_s[G];
     __shared__ int flag_s;
@@ -315,37 +327,50 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
     const int nkeys = k1 - k0;
     const int nsteps = (nkeys + kAttKeys - 1) / kAttKeys;
     const int cur = kv_len - 1;  // the decoded token's row
+    const int cur_step = (cur >= k0 && cur < k1) ? (cur - k0) / kAttKeys : -1;
     const int64_t ks = (int64_t)a.kv_heads * D;
     const __half* kc = reinterpret_cast<const __half*>(a.k_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
     const __half* vc = reinterpret_cast<const __half*>(a.v_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
-    // thread t copies row t & 63 of a step: its key (t < 64) or its value row
-    auto step_bytes = [&](int s) { return (uint32_t)min(kAttKeys, nkeys - s * kAttKeys) * (uint32_t)(4 * D); };
-    // mode 0: every row of step s; 1: all but the decoded token's; 2: only it
-    auto issue = [&](int s, int mode) {
-        const int r = tid & (kAttKeys - 1);
-        const int key = k0 + s * kAttKeys + r;
-        if (key >= k1 || (mode == 1 && key == cur) || (mode == 2 && key != cur)) return;
+    // 16-byte chunk c of a stage: row c / (D/8) (keys, then values), part c % (D/8)
+    constexpr int CPR = D / 8;
+    auto issue = [&](int s, bool skip_cur) {
         uint8_t* base = att_smem + (size_t)(s % kAttStages) * Lay::stage;
-        if (tid < kAttKeys)
-            bulk_g2s(base + r * Lay::kRow, kc + key * ks, 2 * D, &bars[s % kAttStages]);
-        else
-            bulk_g2s(base + kAttKeys * Lay::kRow + r * Lay::vRow, vc + key * ks, 2 * D, &bars[s % kAttStages]);
+        for (int c = tid; c < Lay::chunks; c += kAttThreads) {
+            const int row = c / CPR, part = c - row * CPR;
+            const int r = row & (kAttKeys - 1);
+            const int key = k0 + s * kAttKeys + r;
+            if (key >= k1 || (skip_cur && key == cur)) continue;
+            const __half* src = (row < kAttKeys ? kc : vc) + key * ks + part * 8;
+            cp_async16(base + row * Lay::row + part * 16, src);
+        }
     };
     const int npre = min(kAttStages, nsteps);
     if (tid == 0) {
-        for (int s = 0; s < kAttStages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < kAttStages; ++s) mbar_init(&bars[s], kAttThreads);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int s = 0; s < npre; ++s) mbar_expect_tx(&bars[s], step_bytes(s));
     }
     __syncthreads();
-    for (int s = 0; s < npre; ++s) issue(s, 1);
+    for (int s = 0; s < npre; ++s) {
+        issue(s, true);
+        // the decoded token's rows come after the wait: their copiers arrive then
+        if (s != cur_step || tid >= 2 * CPR) cp_async_arrive(&bars[s]);
+    }
     pdl_trigger();
     pdl_wait();
-    if (cur >= k0 && cur < k1 && (cur - k0) / kAttKeys < npre) issue((cur - k0) / kAttKeys, 2);
-    for (int i = tid; i < G * D; i += kAttThreads) {
-        const int g = i / D, dd = i - g * D;
-        qs[g][dd] = a.q[((int64_t)b * a.heads + kvh * G + g) * D + dd] * a.scale;
+    if (cur_step >= 0 && cur_step < npre && tid < 2 * CPR) {
+        uint8_t* base = att_smem + (size_t)cur_step * Lay::stage;
+        const int r = cur - k0 - cur_step * kAttKeys;
+        const int row = tid < CPR ? r : kAttKeys + r, part = tid < CPR ? tid : tid - CPR;
+        cp_async16(base + row * Lay::row + part * 16, (tid < CPR ? kc : vc) + cur * ks + part * 8);
+        cp_async_arrive(&bars[cur_step]);
     }
+    // this lane's head dims of the G queries, pre-scaled
+    float qr[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j)
+            qr[g][j] = a.q[((int64_t)b * a.heads + kvh * G + g) * D + lane * DPL + j] * a.scale;
     if (tid < G) {
         m_s[tid] = -INFINITY;
         l_s[tid] = 0.0f;
@@ -367,40 +392,44 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
         }
         const int n = min(kAttKeys, k1 - (k0 + s * kAttKeys));
         const uint8_t* kbase = att_smem + (size_t)st * Lay::stage;
-        const uint8_t* vbase = kbase + kAttKeys * Lay::kRow;
-        {  // phase 1: scores of key r for the G heads
-            const int r = warp * 16 + (lane & 15), h = lane >> 4;
-            float sc[G];
+        const uint8_t* vbase = kbase + kAttKeys * Lay::row;
+        // scores: batches of KB keys, transposed across the warp
+        for (int bt = warp; bt < NB; bt += kAttWarps) {
+            float v[32];
 #pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] = 0.0f;
-            if (r < n) {
-                const __half* krow = reinterpret_cast<const __half*>(kbase + r * Lay::kRow) + h * HD;
-#pragma unroll 4
-                for (int dd = 0; dd < HD; dd += 8) {
-                    const uint4 raw = *reinterpret_cast<const uint4*>(krow + dd);
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-                    float kf[8];
+            for (int kk = 0; kk < KB; ++kk) {
+                const __half* kr = reinterpret_cast<const __half*>(kbase + (bt * KB + kk) * Lay::row) + lane * DPL;
+                float kf[DPL];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 f = __half22float2(h2[j]);
-                        kf[2 * j] = f.x;
-                        kf[2 * j + 1] = f.y;
-                    }
+                for (int j = 0; j < DPL; j += 2) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(kr + j));
+                    kf[j] = f.x;
+                    kf[j + 1] = f.y;
+                }
 #pragma unroll
-                    for (int g = 0; g < G; ++g)
+                for (int g = 0; g < G; ++g) {
+                    float t = 0.0f;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) sc[g] = fmaf(qs[g][h * HD + dd + j], kf[j], sc[g]);
+                    for (int j = 0; j < DPL; ++j) t = fmaf(qr[g][j], kf[j], t);
+                    v[kk * G + g] = t;
                 }
             }
 #pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 16);
-            if (lane < 16)
+            for (int o = 16; o >= 1; o >>= 1) {
+                const bool upper = (lane & o) != 0;
 #pragma unroll
-                for (int g = 0; g < G; ++g) ps[r][g] = r < n ? sc[g] : -INFINITY;
+                for (int i = 0; i < o; ++i) {
+                    const float send = upper ? v[i] : v[i + o];
+                    const float keep = upper ? v[i + o] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            const int key = bt * KB + lane / G;
+            ps[key][lane % G] = key < n ? v[0] : -INFINITY;
         }
         __syncthreads();
-        // online softmax bookkeeping: warp w keeps heads w, w + 4, ...
-        for (int g = warp; g < G; g += kAttThreads / 32) {
+        // online softmax bookkeeping: warp w keeps heads w, w + 8, ...
+        for (int g = warp; g < G; g += kAttWarps) {
             const float s0 = ps[lane][g], s1 = ps[lane + 32][g];
             const float mo = m_s[g];
             const float mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
@@ -417,23 +446,20 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
             }
         }
         __syncthreads();
-        if (tid == 0 && s + kAttStages < nsteps) mbar_expect_tx(&bars[st], step_bytes(s + kAttStages));
-        // phase 2: warp w takes keys 16w .. 16w + 15, lanes the head dims
+        // values: warp w takes keys w, w + 8, ... of the stage
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             const float c = corr_s[g];
 #pragma unroll
             for (int j = 0; j < DPL; ++j) acc[g][j] *= c;
         }
-#pragma unroll 4
-        for (int u = 0; u < 16; ++u) {
-            const int r = warp * 16 + u;
-            if (r >= n) continue;  // uniform across the warp
-            const __half* vrow = reinterpret_cast<const __half*>(vbase + r * Lay::vRow) + lane * DPL;
+#pragma unroll 2
+        for (int r = warp; r < n; r += kAttWarps) {
+            const __half* vr = reinterpret_cast<const __half*>(vbase + r * Lay::row) + lane * DPL;
             float vf[DPL];
 #pragma unroll
             for (int j = 0; j < DPL; j += 2) {
-                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vrow + j));
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr + j));
                 vf[j] = f.x;
                 vf[j + 1] = f.y;
             }
@@ -445,7 +471,10 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
             }
         }
         __syncthreads();  // stage st is free again
-        if (s + kAttStages < nsteps) issue(s + kAttStages, 0);
+        if (s + kAttStages < nsteps) {
+            issue(s + kAttStages, false);
+            cp_async_arrive(&bars[st]);
+        }
     }
     if (failed) {
         // let the copies still in flight land before the CTA exits
@@ -454,8 +483,8 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
         if (tid == 0) atomicExch(a.err, 3);
         return;
     }
-    // merge the 4 warps (the ring is idle now)
-    float* wacc = reinterpret_cast<float*>(att_smem);  // [4][G][D]
+    // merge the warps (the ring is idle now)
+    float* wacc = reinterpret_cast<float*>(att_smem);  // [warps][G][D]
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
@@ -463,8 +492,9 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
     __syncthreads();
     for (int i = tid; i < G * D; i += kAttThreads) {
         const int g = i / D, dd = i - g * D;
-        const float o = ((wacc[(0 * G + g) * D + dd] + wacc[(1 * G + g) * D + dd]) + wacc[(2 * G + g) * D + dd]) +
-                        wacc[(3 * G + g) * D + dd];
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttWarps; ++w) o += wacc[(w * G + g) * D + dd];
         const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
         if (a.nsplit == 1) {
             a.out[hb * D + dd] = o * (1.0f / l_s[g]);
@@ -481,41 +511,68 @@ __global__ void __launch_bounds__(kAttThreads) decode_attn_bulk_kernel(const Dec
     if (tid == 0) flag_s = atomic_add_acq_rel_gpu(&a.counters[bk], 1) == a.nsplit - 1;
     __syncthreads();
     if (!flag_s) return;
-    // the last CTA of (b, kvh): split weights exp(m_s - M), then sums in split order
+    // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+    // in split order. The partial sums of a round of 16 splits are requested
+    // first; the split weights are formed while they are in flight.
     const int ns = a.nsplit;
-    float* wts = reinterpret_cast<float*>(att_smem) + 4 * G * D;  // [G][ns]
-    float* inv_l = wts + G * ns;                                   // [G]
-    for (int g = warp; g < G; g += kAttThreads / 32) {
+    float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][16]
+    constexpr int OPT = (G * D + kAttThreads - 1) / kAttThreads;        // outputs per thread
+    float o[OPT];
+#pragma unroll
+    for (int t = 0; t < OPT; ++t) o[t] = 0.0f;
+    // M per head (every thread of a head's warp holds it)
+    for (int g = warp; g < G; g += kAttWarps) {
         const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
         float M = -INFINITY;
         for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hb * ns + s2]));
         M = warp_max(M);
-        float L = 0.0f;
-        for (int s2 = lane; s2 < ns; s2 += 32) {
-            const float mm = __ldcg(&a.part_m[hb * ns + s2]);
-            const float w = mm == -INFINITY ? 0.0f : expf(mm - M);
-            wts[g * ns + s2] = w;
-            L += __ldcg(&a.part_l[hb * ns + s2]) * w;
-        }
-        L = warp_sum(L);
-        if (lane == 0) inv_l[g] = 1.0f / L;
+        if (lane == 0) m_s[g] = M;
+        if (lane == 0) l_s[g] = 0.0f;
     }
     __syncthreads();
-    for (int i = tid; i < G * D; i += kAttThreads) {
+    for (int s0 = 0; s0 < ns; s0 += 16) {
+        const int nr = min(16, ns - s0);
+        float pa[OPT][16];
+#pragma unroll
+        for (int t = 0; t < OPT; ++t) {
+            const int i = tid + t * kAttThreads;
+            const int g = i / D, dd = i - g * D;
+            const int64_t hb = (int64_t)b * a.heads + kvh * G + (g < G ? g : 0);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                pa[t][u] = (i < G * D && u < nr) ? __ldcg(&a.part_acc[(hb * ns + s0 + u) * D + dd]) : 0.0f;
+        }
+        for (int g = warp; g < G; g += kAttWarps) {
+            const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+            float w = 0.0f, lw = 0.0f;
+            if (lane < nr) {
+                const float mm = __ldcg(&a.part_m[hb * ns + s0 + lane]);
+                w = mm == -INFINITY ? 0.0f : expf(mm - m_s[g]);
+                lw = __ldcg(&a.part_l[hb * ns + s0 + lane]) * w;
+            }
+            if (lane < 16) wts[g * 16 + lane] = w;
+            lw = warp_sum(lw);
+            if (lane == 0) l_s[g] += lw;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < OPT; ++t) {
+            const int i = tid + t * kAttThreads;
+            const int g = i / D;
+            if (i < G * D)
+#pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    if (u < nr) o[t] = fmaf(pa[t][u], wts[g * 16 + u], o[t]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int t = 0; t < OPT; ++t) {
+        const int i = tid + t * kAttThreads;
+        if (i >= G * D) continue;
         const int g = i / D, dd = i - g * D;
         const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
-        const float* pa = a.part_acc + hb * ns * D + dd;
-        float o = 0.0f;
-        int s2 = 0;
-        for (; s2 + 8 <= ns; s2 += 8) {
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = __ldcg(pa + (int64_t)(s2 + u) * D);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) o = fmaf(v[u], wts[g * ns + s2 + u], o);
-        }
-        for (; s2 < ns; ++s2) o = fmaf(__ldcg(pa + (int64_t)s2 * D), wts[g * ns + s2], o);
-        a.out[hb * D + dd] = o * inv_l[g];
+        a.out[hb * D + dd] = o[t] * (1.0f / l_s[g]);
     }
     if (tid == 0) a.counters[bk] = 0;
 }
@@ -547,7 +604,7 @@ void launch_attention_rows(const AttnRowsArgs& a, cudaStream_t s) {
     const size_t smem = (size_t)(a.d + a.skv) * sizeof(float);
     if (smem > 200 * 1024) shape_err("attention: key length too long for the single-row kernel");
     if (smem > 48 * 1024)
-        BC_CUDA(cudaFuncSetAttribute(attention_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        allow_max_dynamic_smem(attention_rows_kernel);
     attention_rows_kernel<<<(unsigned)rows, 128, smem, s>>>(a);
     BC_LAUNCHED("attention_rows_kernel");
 }

@@ -53,6 +53,7 @@ struct GemvParams {
     int rtz;
     const float* norm_w;  // persistent kernel only: RMSNorm of each x row fused into the staging
     float norm_eps;
+    QkvEpi qkv;           // EPI_QKV destinations
 };
 
 __device__ __forceinline__ float load_x(const GemvParams& p, int b, int64_t kk) {
@@ -410,6 +411,46 @@ template <int B>
 __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t g, int lane,
                                            const float (&v)[B]) {
     const int64_t row = g * 32 + lane;
+    if (epi == EPI_QKV) {
+        // the whole warp takes part: pairs (2i, 2i+1) are lanes (l, l ^ 1)
+        const QkvEpi& e = p.qkv;
+        const int r = (int)row, half = e.d / 2;
+        const int pos0 = e.pos_ptr ? *e.pos_ptr : e.pos_imm;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const float x = v[b];
+            const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+            if (b >= p.batch || row >= p.n) continue;
+            const int rr = e.row0 + b;
+            const int pos = pos0 + rr * e.pos_step;
+            if (pos < 0 || pos >= e.max_ctx) {  // a device-advanced position ran past the cache
+                atomicExch(e.err, 2);
+                continue;
+            }
+            const int64_t cache_at = (int64_t)rr * e.seq_step * e.cache_sb + (int64_t)pos * e.kd;
+            if (r < e.qd + e.kd) {
+                const int ee = r < e.qd ? r : r - e.qd;
+                const int i = (ee % e.d) / 2;
+                const float c = e.cs[(int64_t)pos * half + i], s = e.sn[(int64_t)pos * half + i];
+                const bool odd = (r & 1) != 0;
+                const float x0 = odd ? partner : x, x1 = odd ? x : partner;
+                const float o = odd ? x0 * s + x1 * c : x0 * c - x1 * s;
+                if (r < e.qd)
+                    e.q[(int64_t)rr * e.qd + ee] = o;
+                else if (e.kv_f16)
+                    static_cast<__half*>(e.kc)[cache_at + ee] = __float2half(o);
+                else
+                    static_cast<float*>(e.kc)[cache_at + ee] = o;
+            } else {
+                const int ee = r - e.qd - e.kd;
+                if (e.kv_f16)
+                    static_cast<__half*>(e.vc)[cache_at + ee] = __float2half(x);
+                else
+                    static_cast<float*>(e.vc)[cache_at + ee] = x;
+            }
+        }
+        return;
+    }
     if (epi == EPI_SWIGLU) {
         // lanes 0..15: gate rows, lanes 16..31: the matching up rows
         const int64_t f = g * 16 + lane;
@@ -535,9 +576,9 @@ void launch_qgemv_t(const GemvLaunch& a) {
     p.rtz = a.rtz ? 1 : 0;
     p.norm_w = nullptr;
     p.norm_eps = 0.0f;
+    p.qkv = a.qkv ? *a.qkv : QkvEpi{};
     auto kern = qgemv_kernel<FMT, MODE, B>;
-    if (pl.smem > 48 * 1024)
-        BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+    if (pl.smem > 48 * 1024) allow_max_dynamic_smem(kern);
     const int64_t grid = a.L->groups() * pl.ksplit;
     launch_kernel(kern, dim3((unsigned)grid), dim3(128), pl.smem, a.s, a.pdl, p, a.epi);
 }

@@ -452,6 +452,7 @@ void launch_qgemv3_t(const LinearPlan& pl, const GemvLaunch& a) {
     p.rtz = a.rtz ? 1 : 0;
     p.norm_w = a.norm_w;
     p.norm_eps = a.norm_eps;
+    p.qkv = a.qkv ? *a.qkv : QkvEpi{};
     q.ktiles = a.L->ktiles();
     q.total_tiles = a.L->groups() * q.ktiles;
     q.total_warps = pl.total_warps;
@@ -461,7 +462,7 @@ void launch_qgemv3_t(const LinearPlan& pl, const GemvLaunch& a) {
     q.counters = a.scratch.counters;
     q.err = a.scratch.err;
     auto kern = qgemv3_kernel<FMT, MODE, B>;
-    BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+    allow_max_dynamic_smem(kern);
     launch_kernel(kern, dim3((unsigned)pl.nctas), dim3(kG3Warps * 32), pl.smem, a.s, a.pdl, q, a.epi);
 }
 

@@ -55,6 +55,13 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
 // memory, which lets the next kernel's CTA start (and fetch its weights)
 // while this one finishes, and GEMVs with many tiles per warp run two CTAs
 // per SM for more warps in flight.
+int device_smem_optin() {
+    int dev = 0, v = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    cuda_check(cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev), "cudaDeviceGetAttribute");
+    return v;
+}
+
 LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
     LinearPlan pl;
     pl.v2 = plan_qgemv(ctx, L, batch, mode);
@@ -88,9 +95,12 @@ size_t LinearPlan::scratch_floats(int batch, const QLayout& L) const {
 
 void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
                    int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,
-                   const GemvScratch& scratch, cudaStream_t s, const float* norm_w, float norm_eps, bool pdl) {
+                   const GemvScratch& scratch, cudaStream_t s, const float* norm_w, float norm_eps, bool pdl,
+                   const QkvEpi* qkv) {
     GemvLaunch a{&plan.v2, &L, w, x, x_f16, x_ld, batch, y, y_ld, epi, res, res_ld, mode, rtz, scratch, s};
     a.pdl = pdl;
+    if (epi == EPI_QKV && !qkv) invalid("fused q/k/v epilogue launched without its destinations");
+    a.qkv = qkv;
     if (!plan.v3) {
         if (norm_w) invalid("the tiled GEMV has no fused RMSNorm; normalise first");
         if (plan.v2.ksplit > 1 &&

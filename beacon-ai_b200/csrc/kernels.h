@@ -11,7 +11,29 @@
 namespace bc {
 
 enum GemvMode { MODE_FAST = 0, MODE_F32 = 1 };
-enum GemvEpilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+enum GemvEpilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+
+// EPI_QKV: the fused q/k/v projection of one decoder layer writes its rows
+// straight to their consumers. Rows [0, qd) are queries, [qd, qd + kd) keys,
+// then kd value rows. Query and key pairs (2i, 2i+1) of each head are rotated
+// at the row's position (RoPE with interleaved pairs, rope.rs:10-60): queries
+// go to q[row][qd] as f32, keys and values to the caches at [seq][pos].
+// Batch row b of the launch is model row row0 + b, at position
+// *pos_ptr (or pos_imm) + row * pos_step, in sequence row * seq_step; a
+// position outside [0, max_ctx) sets *err = 2 and writes nothing.
+struct QkvEpi {
+    float* q = nullptr;
+    void* kc = nullptr;
+    void* vc = nullptr;
+    int kv_f16 = 1;
+    const float* cs = nullptr;  // rope tables [max_ctx][d / 2]
+    const float* sn = nullptr;
+    int qd = 0, kd = 0, d = 0;
+    int64_t cache_sb = 0;
+    const int* pos_ptr = nullptr;
+    int pos_imm = 0, pos_step = 0, seq_step = 0, row0 = 0, max_ctx = 0;
+    int* err = nullptr;
+};
 
 // Scratch for split-K GEMV: partial sums and one arrival counter per 32-row
 // group. Counters must be zero before the first launch; every launch leaves
@@ -62,6 +84,7 @@ struct GemvLaunch {
     const float* norm_w = nullptr;  // fused RMSNorm weight (persistent kernel only)
     float norm_eps = 0.0f;
     bool pdl = false;               // launch with programmatic stream serialisation
+    const QkvEpi* qkv = nullptr;    // EPI_QKV destinations
 };
 
 // cudaLaunchKernelEx with programmatic stream serialisation when `pdl`.
@@ -79,6 +102,18 @@ void launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, c
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     cuda_check(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), "cudaLaunchKernelEx");
+}
+// Opt a kernel in to the device's largest dynamic shared memory. Kernels
+// launched with several sizes (and captured into graphs) are covered for all
+// of them, whichever launch set the attribute last.
+int device_smem_optin();
+template <typename... KArgs>
+void allow_max_dynamic_smem(void (*kern)(KArgs...)) {
+    cudaFuncAttributes fa;
+    cuda_check(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes");
+    cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    device_smem_optin() - (int)fa.sharedSizeBytes),
+               "cudaFuncSetAttribute");
 }
 void launch_qgemv_q4_0(const GemvLaunch& a);
 void launch_qgemv_q8_0(const GemvLaunch& a);
@@ -99,7 +134,7 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
 void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
                    int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,
                    const GemvScratch& scratch, cudaStream_t s, const float* norm_w = nullptr, float norm_eps = 0.0f,
-                   bool pdl = false);
+                   bool pdl = false, const QkvEpi* qkv = nullptr);
 void launch_qgemv3_q4_0(const LinearPlan& pl, const GemvLaunch& a);
 void launch_qgemv3_q8_0(const LinearPlan& pl, const GemvLaunch& a);
 void launch_qgemv3_q4_k(const LinearPlan& pl, const GemvLaunch& a);

@@ -37,8 +37,6 @@ constexpr int kPrefillChunk = 512;
 
 // --- small kernels ------------------------------------------------------------
 
-__device__ __forceinline__ int read_pos(const int* pos_ptr, int pos_imm) { return pos_ptr ? *pos_ptr : pos_imm; }
-
 // h[row] = E[tok[row]] (f32). Out-of-range ids write zeros and raise *err.
 __global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hid, const int32_t* tok, float* h,
                              int* err) {
@@ -109,48 +107,6 @@ __global__ void rope_table_kernel(float* cs, float* sn, int max_ctx, int d, floa
     sincosf(angle, &s, &c);
     cs[idx] = c;
     sn[idx] = s;
-}
-
-// qkv [rows][qd + 2 kd] -> q [rows][qd] (roped), K/V cache rows (k roped).
-// Row r is sequence (seq0 + r*seq_step) at position pos + r*pos_step.
-template <typename KV>
-__global__ void qkv_post_kernel(const float* qkv, float* q, KV* kc, KV* vc, const float* cs, const float* sn,
-                                int rows, int qd, int kd, int d, int64_t cache_sb, const int* pos_ptr, int pos_imm,
-                                int pos_step, int seq_step, int max_ctx, int* err) {
-    pdl_trigger();
-    pdl_wait();
-    const int r = blockIdx.y;
-    const int pos0 = read_pos(pos_ptr, pos_imm);
-    const int pos = pos0 + r * pos_step;
-    if (pos < 0 || pos >= max_ctx) {  // a device-advanced position ran past the cache
-        if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 2);
-        return;
-    }
-    const int seq = r * seq_step;
-    const int qkvn = qd + 2 * kd;
-    const float* src = qkv + (int64_t)r * qkvn;
-    const int half = d / 2;
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < qd / 2 + kd / 2 + kd / 2; j += gridDim.x * blockDim.x) {
-        if (j < qd / 2) {  // q pair
-            const int e = 2 * j, i = (e % d) / 2;
-            const float c = cs[(int64_t)pos * half + i], s = sn[(int64_t)pos * half + i];
-            const float x0 = src[e], x1 = src[e + 1];
-            q[(int64_t)r * qd + e] = x0 * c - x1 * s;
-            q[(int64_t)r * qd + e + 1] = x0 * s + x1 * c;
-        } else if (j < qd / 2 + kd / 2) {  // k pair
-            const int e = 2 * (j - qd / 2), i = (e % d) / 2;
-            const float c = cs[(int64_t)pos * half + i], s = sn[(int64_t)pos * half + i];
-            const float x0 = src[qd + e], x1 = src[qd + e + 1];
-            KV* dst = kc + (int64_t)seq * cache_sb + (int64_t)pos * kd + e;
-            dst[0] = (KV)(x0 * c - x1 * s);
-            dst[1] = (KV)(x0 * s + x1 * c);
-        } else {  // v pair
-            const int e = 2 * (j - qd / 2 - kd / 2);
-            KV* dst = vc + (int64_t)seq * cache_sb + (int64_t)pos * kd + e;
-            dst[0] = (KV)src[qd + kd + e];
-            dst[1] = (KV)src[qd + kd + e + 1];
-        }
-    }
 }
 
 // [parts][rows][per] -> [rows][parts*per]
@@ -245,14 +201,20 @@ int gemv_mode(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_
 bool gemv_rtz(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_NUMERICS_REF_RTZ; }
 
 // y = W x over `rows` rows of x, in chunks of 16 rows (the GEMV batch limit).
+// qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
-            int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s) {
+            int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s, const QkvEpi* qkv = nullptr) {
     for (int r0 = 0; r0 < rows; r0 += 16) {
         const int b = std::min(16, rows - r0);
         LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
+        QkvEpi qe;
+        if (qkv) {
+            qe = *qkv;
+            qe.row0 = r0;
+        }
         launch_linear(pl, L, w, x + (int64_t)r0 * x_ld, false, x_ld, b, y + (int64_t)r0 * y_ld, y_ld, epi,
                       res ? res + (int64_t)r0 * res_ld : nullptr, res_ld, gemv_mode(m), gemv_rtz(m), m->gsc, s,
-                      nullptr, 0.0f, m->pdl);
+                      nullptr, 0.0f, m->pdl, qkv ? &qe : nullptr);
     }
 }
 
@@ -264,20 +226,25 @@ void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int
 // y = W rmsnorm(x, norm_w): the norm rides in the persistent GEMV's staging
 // when every row chunk takes that kernel, otherwise it runs on its own first.
 void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, const float* norm_w, int rows,
-                   float* y, int64_t y_ld, int epi, cudaStream_t s) {
+                   float* y, int64_t y_ld, int epi, cudaStream_t s, const QkvEpi* qkv = nullptr) {
     const int64_t hid = m->cfg.hidden_size;
     bool fused = true;
     for (int r0 = 0; r0 < rows && fused; r0 += 16) fused = plan_linear(m->ctx, L, std::min(16, rows - r0), gemv_mode(m)).v3;
     if (!fused) {
         rmsnorm(m, x, norm_w, m->xn, rows, s);
-        linear(m, L, w, m->xn, hid, rows, y, y_ld, epi, nullptr, 0, s);
+        linear(m, L, w, m->xn, hid, rows, y, y_ld, epi, nullptr, 0, s, qkv);
         return;
     }
     for (int r0 = 0; r0 < rows; r0 += 16) {
         const int b = std::min(16, rows - r0);
         LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
+        QkvEpi qe;
+        if (qkv) {
+            qe = *qkv;
+            qe.row0 = r0;
+        }
         launch_linear(pl, L, w, x + (int64_t)r0 * hid, false, hid, b, y + (int64_t)r0 * y_ld, y_ld, epi, nullptr, 0,
-                      gemv_mode(m), gemv_rtz(m), m->gsc, s, norm_w, m->cfg.rms_norm_eps, m->pdl);
+                      gemv_mode(m), gemv_rtz(m), m->gsc, s, norm_w, m->cfg.rms_norm_eps, m->pdl, qkv ? &qe : nullptr);
     }
 }
 
@@ -292,23 +259,27 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
     const int64_t cache_sb = (int64_t)c.max_context * m->kd;
     for (int li = 0; li < c.num_layers; ++li) {
         LayerW& L = m->layers[li];
-        normed_linear(m, m->Lqkv, L.wqkv->ptr, m->h, static_cast<const float*>(L.attn_norm->ptr), rows, m->qkv,
-                      m->qkv_n, EPI_STORE, s);
         {
-            dim3 grid(cdiv(m->qd / 2 + m->kd, 256), rows);
-            const int pos_step = decode ? 0 : 1, seq_step = decode ? 1 : 0;
-            const float* cs = static_cast<const float*>(m->rope_cs->ptr);
-            const float* sn = static_cast<const float*>(m->rope_sn->ptr);
-            if (f16kv)
-                launch_kernel(qkv_post_kernel<__half>, grid, dim3(256), 0, s, m->pdl, (const float*)m->qkv, m->q,
-                              static_cast<__half*>(L.kc->ptr), static_cast<__half*>(L.vc->ptr), cs, sn, rows,
-                              (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step,
-                              (int)c.max_context, m->err_dev);
-            else
-                launch_kernel(qkv_post_kernel<float>, grid, dim3(256), 0, s, m->pdl, (const float*)m->qkv, m->q,
-                              static_cast<float*>(L.kc->ptr), static_cast<float*>(L.vc->ptr), cs, sn, rows,
-                              (int)m->qd, (int)m->kd, D, cache_sb, pos_ptr, pos_imm, pos_step, seq_step,
-                              (int)c.max_context, m->err_dev);
+            // q/k/v projection with RoPE and the KV cache write in its epilogue
+            QkvEpi qe;
+            qe.q = m->q;
+            qe.kc = L.kc->ptr;
+            qe.vc = L.vc->ptr;
+            qe.kv_f16 = f16kv ? 1 : 0;
+            qe.cs = static_cast<const float*>(m->rope_cs->ptr);
+            qe.sn = static_cast<const float*>(m->rope_sn->ptr);
+            qe.qd = (int)m->qd;
+            qe.kd = (int)m->kd;
+            qe.d = D;
+            qe.cache_sb = cache_sb;
+            qe.pos_ptr = pos_ptr;
+            qe.pos_imm = pos_imm;
+            qe.pos_step = decode ? 0 : 1;
+            qe.seq_step = decode ? 1 : 0;
+            qe.max_ctx = (int)c.max_context;
+            qe.err = m->err_dev;
+            normed_linear(m, m->Lqkv, L.wqkv->ptr, m->h, static_cast<const float*>(L.attn_norm->ptr), rows, m->qkv,
+                          m->qkv_n, EPI_QKV, s, &qe);
         }
         const float scale = 1.0f / sqrtf((float)D);  // engine.rs:415
         if (decode) {
