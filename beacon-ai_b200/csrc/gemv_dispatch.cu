@@ -4,6 +4,7 @@
 #include <algorithm>
 
 #include "gemv3.cuh"
+#include "qgemm_tc.h"
 
 namespace bc {
 
@@ -142,14 +143,21 @@ GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const LinearPlan& pl, i
     return sc;
 }
 
-// Prefill-sized matmul through the GEMV in 16-row chunks (each chunk streams
-// the weight once). Numerics follow the context's mode exactly.
+// Prefill-sized matmul: the tensor-core GEMM in the fast numerics, otherwise
+// the GEMV in 16-row chunks (each chunk streams the weight once), which
+// follows the exact and CPU-reproducing numerics to the bit.
 void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTensor* w, const void* x, bool x_f16,
                    int64_t rows, float* out, int numerics) {
     const int mode = numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32;
     const bool rtz = numerics == BEACON_CUDA_NUMERICS_REF_RTZ;
     const QLayout& L = w->q;
     const size_t eb = x_f16 ? 2 : 4;
+    if (mode == MODE_FAST && qgemm_tc_supported(L)) {
+        void* x16 = ctx->ws.get(qgemm_tc_scratch_bytes(rows, L.k), s);
+        launch_qgemm_tc(L, w->data(), x, x_f16, L.k, rows, out, L.n, EPI_STORE, nullptr, 0, false, ctx->ws.flags() + 1, s,
+                        x16);
+        return;
+    }
     for (int64_t r0 = 0; r0 < rows; r0 += 16) {
         const int b = (int)std::min<int64_t>(16, rows - r0);
         LinearPlan pl = plan_linear(ctx, L, b, mode);

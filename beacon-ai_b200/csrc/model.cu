@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "qgemm_tc.h"
 
 namespace bc {
 
@@ -179,6 +180,7 @@ struct BeaconCudaModel {
     // scratch
     bc::GemvScratch gsc;
     std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
+    std::unique_ptr<bc::DeviceBuffer> x16;  // f16 activations of the prefill GEMM
     int attn_nsplit = 1;
     float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
     int* attn_cnt = nullptr;
@@ -202,8 +204,19 @@ bool gemv_rtz(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_
 
 // y = W x over `rows` rows of x, in chunks of 16 rows (the GEMV batch limit).
 // qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.
+// More than 16 rows in the fast numerics run as one tensor-core GEMM.
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
             int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s, const QkvEpi* qkv = nullptr) {
+    if (rows > 16 && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L)) {
+        QkvEpi qe;
+        if (qkv) {
+            qe = *qkv;
+            qe.row0 = 0;
+        }
+        launch_qgemm_tc(L, w, x, false, x_ld, rows, y, y_ld, epi, res, res_ld, false, m->err_dev, s, m->x16->ptr,
+                        qkv ? &qe : nullptr);
+        return;
+    }
     for (int r0 = 0; r0 < rows; r0 += 16) {
         const int b = std::min(16, rows - r0);
         LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
@@ -386,6 +399,7 @@ void check_err(BeaconCudaModel* m, cudaStream_t s) {
         BC_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), s));
         if (herr == 2) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
         if (herr == 3) fail(BEACON_CUDA_ERR_CUDA, "decode attention: a bounded wait for the KV cache copies gave up");
+        if (herr == 4) fail(BEACON_CUDA_ERR_CUDA, "tensor-core GEMM: a bounded pipeline wait gave up");
         shape_err("token id out of range for the vocabulary");
     }
 }
@@ -531,6 +545,9 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
                o_ll = carve(R * m->v_loc), o_la = carve(tp > 1 ? R * Vt : 64), o_lg = carve(tp > 1 ? R * Vt : 64),
                o_tok = carve(R), o_next = carve(R), o_pos = carve(64);
         m->act = std::make_unique<DeviceBuffer>(floats * 4);
+        // f16 activations of the prefill GEMM (largest K: hidden, q width or FFN shard)
+        m->x16 = std::make_unique<DeviceBuffer>(
+            qgemm_tc_scratch_bytes(R, std::max<int64_t>(c.hidden_size, std::max<int64_t>(m->qd, m->f_loc))));
         BC_CUDA(cudaMemset(m->act->ptr, 0, floats * 4));
         float* base = static_cast<float*>(m->act->ptr);
         m->h = base + o_h;
