@@ -201,6 +201,26 @@ def test_batched_decode_equals_single_sequences(be):
             assert np.abs(lg[b] - single[b][p]).max() <= 1e-4
 
 
+def test_batch32_decode_on_the_gemm_matches_single_sequences(be):
+    """Batch 32 (the 8B-shape batched-decode config): more than 16 rows take the
+    tensor-core GEMM for every linear; each sequence's logits stay within the
+    logits bar of the same sequence decoded alone (GEMV path)."""
+    from beacon_cuda import _lib as L
+    c = small_cfg(num_layers=2, max_context=16)
+    w = make_weights(oracle_cfg(c), orc.Q4_K, seed=63)
+    B = 32
+    mb = cuda_model(be, c, w, numerics=L.NUMERICS_FAST, kv_dtype=L.DTYPE_F16, max_batch=B)
+    ms = cuda_model(be, c, w, numerics=L.NUMERICS_FAST, kv_dtype=L.DTYPE_F16, max_batch=1)
+    rng = np.random.default_rng(64)
+    toks = rng.integers(0, c["vocab_size"], size=(B, 3)).tolist()
+    batched = [mb.decode_step([seq[p] for seq in toks], p, want_logits=True)[1] for p in range(3)]
+    for b in (0, 7, 19, 31):
+        ms.reset()
+        for p in range(3):
+            lg = ms.decode_step([toks[b][p]], p, want_logits=True)[1][0]
+            assert np.abs(batched[p][b] - lg).max() <= LOGITS_TOL, (b, p)
+
+
 def test_context_overflow_and_bad_tokens(be):
     from beacon_cuda import ContextOverflow, ShapeMismatch
     from beacon_cuda import _lib as L
