@@ -32,12 +32,15 @@ static void nccl_wait(ncclComm_t comm, int timeout_ms, const char* what) {
             ncclCommAbort(comm);
             nccl_check(st, what);
         }
-        auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
-        if (ms > timeout_ms) {
+        const auto us =
+            std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (us > (int64_t)timeout_ms * 1000) {
             ncclCommAbort(comm);
             fail(BEACON_CUDA_ERR_COMM, std::string(what) + ": timed out");
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        // an enqueue finishes within microseconds; an initialisation takes longer
+        if (us > 1000) std::this_thread::sleep_for(std::chrono::microseconds(200));
+        else std::this_thread::yield();
     }
 }
 
@@ -48,10 +51,13 @@ void comm_destroy(BeaconCudaContext* ctx) {
     }
 }
 
+// The communicator is non-blocking (bounded initialisation), so every call may
+// return ncclInProgress and must have finished enqueueing before the next one.
 void comm_all_reduce_sum(BeaconCudaContext* ctx, float* buf, size_t count, cudaStream_t s) {
     if (ctx->nranks <= 1) return;
-    nccl_check(ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->comm), s),
-               "ncclAllReduce");
+    ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+    nccl_check(ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
+    nccl_wait(comm, ctx->comm_timeout_ms, "ncclAllReduce");
 }
 
 void comm_all_gather(BeaconCudaContext* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
@@ -59,7 +65,9 @@ void comm_all_gather(BeaconCudaContext* ctx, const float* send, float* recv, siz
         if (send != recv) BC_CUDA(cudaMemcpyAsync(recv, send, count * 4, cudaMemcpyDeviceToDevice, s));
         return;
     }
-    nccl_check(ncclAllGather(send, recv, count, ncclFloat32, static_cast<ncclComm_t>(ctx->comm), s), "ncclAllGather");
+    ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+    nccl_check(ncclAllGather(send, recv, count, ncclFloat32, comm, s), "ncclAllGather");
+    nccl_wait(comm, ctx->comm_timeout_ms, "ncclAllGather");
 }
 
 }  // namespace bc
@@ -112,7 +120,6 @@ int32_t beacon_cuda_op_all_reduce_f32(BeaconCudaContext* ctx, BeaconCudaStream* 
         if (t->dtype != BEACON_CUDA_DTYPE_F32) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "all_reduce: F32 only");
         set_device(ctx);
         comm_all_reduce_sum(ctx, static_cast<float*>(t->data()), (size_t)t->numel(), stream->s);
-        if (ctx->nranks > 1) nccl_wait(static_cast<ncclComm_t>(ctx->comm), ctx->comm_timeout_ms, "ncclAllReduce");
         return BEACON_CUDA_OK;
     });
 }

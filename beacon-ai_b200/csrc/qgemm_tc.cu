@@ -72,7 +72,7 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
 constexpr uint32_t kTcIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
                               ((uint32_t)(kTcHalf >> 4) << 24);
 
-// 2-D tensor copy (no multicast) of one box into shared memory.
+// 2-D tensor copy of one box into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
