@@ -34,7 +34,7 @@ namespace bc {
 
 namespace {
 
-constexpr int kPrefillChunk = 512;
+constexpr int kPrefillChunk = 2048;
 
 // --- small kernels ------------------------------------------------------------
 

@@ -328,7 +328,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
     // 1024-byte aligned ring (the swizzle pattern follows address bits 4-9)
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t m0 = (int64_t)blockIdx.y * kTcBM, n0 = (int64_t)blockIdx.x * kTcBN;
+    // consecutive CTAs share a weight tile (x runs over the row tiles), so each
+    // weight slice comes from HBM once and from L2 for the other row tiles
+    const int64_t m0 = (int64_t)blockIdx.x * kTcBM, n0 = (int64_t)blockIdx.y * kTcBN;
     const int nkb = (int)((p.k + kTcBK - 1) / kTcBK);
     if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
@@ -502,7 +504,7 @@ template <int FMT>
 void launch_tc_t(const TcParams& p, const CUtensorMap& map, cudaStream_t s) {
     auto kern = qgemm_tc_kernel<FMT>;
     allow_max_dynamic_smem(kern);
-    dim3 grid((unsigned)((p.n + kTcBN - 1) / kTcBN), (unsigned)((p.m + kTcBM - 1) / kTcBM));
+    dim3 grid((unsigned)((p.m + kTcBM - 1) / kTcBM), (unsigned)((p.n + kTcBN - 1) / kTcBN));
     kern<<<grid, kTcThreads, kTcSmem, s>>>(p, map);
     BC_LAUNCHED("qgemm_tc_kernel");
 }
@@ -521,7 +523,7 @@ void launch_qgemm_tc(const QLayout& L, const void* w, const void* x, bool x_f16,
     if (rows <= 0) return;
     if (!qgemm_tc_supported(L)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "tensor-core GEMM: unsupported block type");
     if (epi == EPI_QKV && !qkv) invalid("fused q/k/v epilogue launched without its destinations");
-    if (rows > (int64_t)65535 * kTcBM) invalid("tensor-core GEMM: too many rows");
+    if ((L.n + kTcBN - 1) / kTcBN > 65535) invalid("tensor-core GEMM: too many output columns");
     const __half* xh = static_cast<const __half*>(x);
     int64_t ld = x_ld;
     if (!x_f16 || (reinterpret_cast<uintptr_t>(x) & 15) || (x_ld * 2) % 16) {

@@ -42,6 +42,10 @@ WORKLOADS = {
     "llama3-70b-q4k-tp": dict(shape="LLAMA3_70B", context=8192, batch=1,
                               name="Llama-3-70B-shape decoder, Q4_K linears, f16 KV, tensor-parallel, batch 1, "
                                    "context 8192, greedy decode"),
+    # prefill (time to first token); its own line, not the decode metric
+    "llama3-8b-q8_0-prefill": dict(shape="LLAMA3_8B", context=2048, batch=4,
+                                   name="Llama-3-8B-shape decoder, Q8_0 linears, f16 KV, prefill of 4 x 2048-token "
+                                        "prompts (time to first token)"),
 }
 METRIC = "decode tok/s"
 
@@ -59,6 +63,8 @@ def parse():
                    help="profiling only: build the workload with this many layers (the line says so)")
     p.add_argument("--profile-run", action="store_true",
                    help="profiling only: run warm-up and timed steps, skip the e2e, roofline and CPU legs")
+    p.add_argument("--prefill", action="store_true",
+                   help="measure prefill instead: 4 x 2048-token prompts through the tensor-core GEMM (one JSON line)")
     a = p.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -346,7 +352,7 @@ def run_ours(a):
         "gpu_launches": launches * a.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "qgemv_kernel<Q4_K, FAST, B=%d> (fused gate/up + SwiGLU), %.2f us/launch, "
+                     "kernel": "qgemv3_kernel<Q4_K, FAST, B=%d> (fused gate/up + SwiGLU), %.2f us/launch, "
                                "%d algorithmic bytes/launch, peak %s" % (batch, us, nbytes, peak_kind)},
     }
     if clk:
@@ -365,6 +371,81 @@ def run_ours(a):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def run_prefill(a):
+    """Prefill of config 4: 4 prompts x 2048 tokens, Q8_0 8B shape, one GPU.
+    value = prompt tokens/s over the batch; ttft_ms = time to prefill all four.
+    roofline: the fused gate/up dequant-GEMM at M = 2048 through the C-ABI op,
+    FLOPs 2*M*N*K over CUDA-event time, against the measured bf16 peak."""
+    import numpy as np
+    import torch
+
+    from beacon_cuda import CudaBackend, CudaModel, DecoderConfig
+    from beacon_cuda import _lib as L
+    from beacon_cuda.synthetic import load_synthetic
+
+    wl = "llama3-8b-q8_0-prefill"
+    shp = shape_of(wl)
+    if a.layers:
+        shp["num_layers"] = a.layers
+    P, NB = WORKLOADS[wl]["context"], WORKLOADS[wl]["batch"]
+    be = CudaBackend(0, L.NUMERICS_FAST)
+    model = CudaModel(be, DecoderConfig(**shp, max_context=P + 16, max_batch=1, numerics=L.NUMERICS_FAST,
+                                        kv_dtype=L.DTYPE_F16))
+    load_synthetic(model, L.DTYPE_Q8_0, seed=0)
+    rng = np.random.default_rng(0)
+    prompts = rng.integers(0, shp["vocab_size"], size=(NB, P)).tolist()
+    ts = torch.cuda.ExternalStream(model.stream.cuda_stream)
+    for i in range(min(a.warmup, 3)):
+        model.forward(prompts[i % NB], 0, want_logits=False)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(a.steps, 4))
+    e0.record(ts)
+    for _ in range(steps):
+        for b in range(NB):
+            model.forward(prompts[b], 0, want_logits=False)
+    e1.record(ts)
+    e1.synchronize()
+    ttft_ms = e0.elapsed_time(e1) / steps
+    value = NB * P / (ttft_ms / 1e3)
+
+    # GEMM roofline: gate/up (2F x H) at M = P rows
+    H, F = shp["hidden_size"], shp["intermediate_size"]
+    st = be.new_stream()
+    w = be.quantize(st, be.upload((rng.standard_normal((2 * F, H), dtype=np.float32) * 0.02)), L.DTYPE_Q8_0)
+    x = be.upload(rng.standard_normal((P, H), dtype=np.float32))
+    gs = torch.cuda.ExternalStream(st.cuda_stream)
+    for _ in range(2):
+        be.quantized_matmul(st, x, w)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    g0.record(gs)
+    for _ in range(reps):
+        be.quantized_matmul(st, x, w)
+    g1.record(gs)
+    g1.synchronize()
+    gemm_us = g0.elapsed_time(g1) * 1e3 / reps
+    tflops = 2.0 * P * (2 * F) * H / (gemm_us * 1e-6) / 1e12
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak, peak_kind = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    out = {"metric": "prefill tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
+           "warmup": min(a.warmup, 3), "ms_per_step": round(ttft_ms, 3), "ttft_ms": round(ttft_ms, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights, f16 MMA, f32 accumulate",
+           "data": "synthetic (seeded random weights and prompt tokens)",
+           "config": {"workload": WORKLOADS[wl]["name"] + (f" (REDUCED to {a.layers} layers)" if a.layers else ""),
+                      "model_shape": wl, "batch": NB, "prompt": P, "parallelism": "tp1"},
+           "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tflops / peak, 4), "traffic": None,
+                        "kernel": "qgemm_tc_kernel<Q8_0> (fused gate/up, M=%d N=%d K=%d), %.1f us/launch incl. the "
+                                  "f16 activation copy, peak %s (dense bf16)" % (P, 2 * F, H, gemm_us, peak_kind)}}
+    model.close()
+    del model
+    be.close()
+    print(json.dumps(out), flush=True)
 
 
 def run_reference(a):
@@ -398,5 +479,7 @@ if __name__ == "__main__":
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.prefill:
+        run_prefill(args)
     else:
         run_ours(args)
