@@ -270,6 +270,191 @@ __global__ void decode_attn_combine_kernel(const DecodeAttnArgs a, int d) {
     }
 }
 
+// Prefill attention, tiled -----------------------------------------------------------
+// One CTA (8 warps) per (tile of 128/G query rows, KV head): the G query heads
+// of the KV head make 128 (row, head) pairs that share every key/value tile
+// staged in shared memory (64 keys at a time), so each K/V row is read once
+// per CTA instead of once per query. Scores: thread t owns pairs 4(t/8) ..
+// +3 and keys 8(t%8) .. +7 of a tile; the online softmax (engine.rs:415-440
+// semantics: max-subtracted exp, normalised at the end) reduces over the 8
+// threads of a pair group with shuffles; the same thread then owns those
+// pairs' outputs for dims (t%8) D/8 .. +D/8, so the rescale stays local.
+// f32 arithmetic; used for prefill in the fast numerics (the row kernel above
+// keeps the reference's summation order for the exact ones).
+constexpr int kPfKeys = 64;
+constexpr int kPfPairs = 128;
+constexpr int kPfThreads = 256;
+
+template <int D>
+struct PfLayout {
+    static constexpr int kT = kPfKeys + 4;   // transposed key tile row (padded): [D][kT]
+    static constexpr int q = D * kPfPairs;   // qsT [D][pairs]
+    static constexpr int k = D * kT;         // ksT [D][kT]
+    static constexpr int v = kPfKeys * D;    // vs  [keys][D]
+    static constexpr int p = kPfKeys * kPfPairs;  // psT [keys][pairs]
+    static constexpr size_t bytes = (size_t)(q + k + v + p) * 4;
+};
+
+template <int D, int G, typename KV>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const AttnRowsArgs a) {
+    using Lay = PfLayout<D>;
+    constexpr int RT = kPfPairs / G;  // query rows per CTA
+    constexpr int DPT = D / 8;        // output dims per thread
+    extern __shared__ __align__(16) float pf_smem[];
+    float* qsT = pf_smem;
+    float* ksT = qsT + Lay::q;
+    float* vs = ksT + Lay::k;
+    float* psT = vs + Lay::v;
+    const int tid = threadIdx.x;
+    const int kvh = blockIdx.y;
+    const int64_t r0 = (int64_t)blockIdx.x * RT;
+    const int pg = tid >> 3, kg = tid & 7;  // pair group (4 pairs), key / dim group
+    // q tile, pre-scaled, transposed: qsT[d][pair], pair = row * G + g
+    for (int i = tid; i < kPfPairs * D; i += kPfThreads) {
+        const int pr = i / D, d = i - pr * D;
+        const int64_t row = r0 + pr / G;
+        const int h = kvh * G + pr % G;
+        float v = 0.0f;
+        if (row < a.sq) v = reinterpret_cast<const float*>(a.q)[h * a.q_sh + row * a.q_ss + d] * a.scale;
+        qsT[d * kPfPairs + pr] = v;
+    }
+    float m[4], l[4], acc[4][DPT];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) acc[j][e] = 0.0f;
+    }
+    // keys [0, skv); causal: row s sees keys <= skv - sq + s
+    const int64_t last_row = min((int64_t)a.sq - 1, r0 + RT - 1);
+    const int64_t kend = a.causal ? min((int64_t)a.skv, a.skv - a.sq + last_row + 1) : (int64_t)a.skv;
+    const KV* kbase = reinterpret_cast<const KV*>(a.k) + (int64_t)kvh * a.kv_sh;
+    const KV* vbase = reinterpret_cast<const KV*>(a.v) + (int64_t)kvh * a.kv_sh;
+    for (int64_t k0 = 0; k0 < kend; k0 += kPfKeys) {
+        __syncthreads();  // previous tile fully consumed
+        for (int i = tid; i < kPfKeys * D; i += kPfThreads) {
+            const int kk = i / D, d = i - kk * D;
+            const int64_t key = k0 + kk;
+            float kv = 0.0f, vv = 0.0f;
+            if (key < kend) {
+                if (sizeof(KV) == 2) {
+                    kv = __half2float(reinterpret_cast<const __half*>(kbase)[key * a.kv_ss + d]);
+                    vv = __half2float(reinterpret_cast<const __half*>(vbase)[key * a.kv_ss + d]);
+                } else {
+                    kv = reinterpret_cast<const float*>(kbase)[key * a.kv_ss + d];
+                    vv = reinterpret_cast<const float*>(vbase)[key * a.kv_ss + d];
+                }
+            }
+            ksT[d * Lay::kT + kk] = kv;
+            vs[kk * D + d] = vv;
+        }
+        __syncthreads();
+        // scores s[4 pairs][8 keys]
+        float s[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s[j][e] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < D; ++d) {
+            const float4 q4 = *reinterpret_cast<const float4*>(qsT + d * kPfPairs + pg * 4);
+            const float4 ka = *reinterpret_cast<const float4*>(ksT + d * Lay::kT + kg * 8);
+            const float4 kb = *reinterpret_cast<const float4*>(ksT + d * Lay::kT + kg * 8 + 4);
+            const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+            const float kv8[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s[j][e] = fmaf(qv[j], kv8[e], s[j][e]);
+        }
+        // mask, online softmax over the 8 threads of the pair group
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int pr = pg * 4 + j;
+            const int64_t row = r0 + pr / G;
+            const int64_t lim = a.causal ? (int64_t)a.skv - a.sq + row : (int64_t)a.skv - 1;  // last visible key
+            float mx = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int64_t key = k0 + kg * 8 + e;
+                if (key > lim || key >= kend) s[j][e] = -INFINITY;
+                mx = fmaxf(mx, s[j][e]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            const float mn = fmaxf(m[j], mx);
+            const float c = (m[j] == -INFINITY) ? 0.0f : expf(m[j] - mn);
+            float sum = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float pv = mn == -INFINITY ? 0.0f : expf(s[j][e] - mn);
+                s[j][e] = pv;
+                sum += pv;
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            l[j] = l[j] * c + sum;
+            m[j] = mn;
+#pragma unroll
+            for (int e = 0; e < DPT; ++e) acc[j][e] *= c;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            *reinterpret_cast<float4*>(psT + (kg * 8 + e) * kPfPairs + pg * 4) =
+                make_float4(s[0][e], s[1][e], s[2][e], s[3][e]);
+        __syncthreads();
+        // acc[4 pairs][DPT dims] += P V
+        const int kn = (int)min((int64_t)kPfKeys, kend - k0);
+        for (int kk = 0; kk < kn; ++kk) {
+            const float4 p4 = *reinterpret_cast<const float4*>(psT + kk * kPfPairs + pg * 4);
+            const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+            float vv[DPT];
+#pragma unroll
+            for (int e = 0; e < DPT; e += 4) {
+                const float4 t4 = *reinterpret_cast<const float4*>(vs + kk * D + kg * DPT + e);
+                vv[e] = t4.x;
+                vv[e + 1] = t4.y;
+                vv[e + 2] = t4.z;
+                vv[e + 3] = t4.w;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int e = 0; e < DPT; ++e) acc[j][e] = fmaf(pv[j], vv[e], acc[j][e]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int pr = pg * 4 + j;
+        const int64_t row = r0 + pr / G;
+        if (row >= a.sq) continue;
+        const int h = kvh * G + pr % G;
+        const float inv = l[j] > 0.0f ? 1.0f / l[j] : 0.0f;
+        float* o = a.out + h * a.o_sh + row * a.o_ss + kg * DPT;
+#pragma unroll
+        for (int e = 0; e < DPT; e += 4)
+            *reinterpret_cast<float4*>(o + e) =
+                make_float4(acc[j][e] * inv, acc[j][e + 1] * inv, acc[j][e + 2] * inv, acc[j][e + 3] * inv);
+    }
+}
+
+template <int D, int G>
+void launch_prefill_t(const AttnRowsArgs& a, cudaStream_t s) {
+    constexpr int RT = kPfPairs / G;
+    dim3 grid((unsigned)((a.sq + RT - 1) / RT), (unsigned)a.kv_heads);
+    if (a.kv_f16) {
+        allow_max_dynamic_smem(prefill_attn_kernel<D, G, __half>);
+        prefill_attn_kernel<D, G, __half><<<grid, kPfThreads, PfLayout<D>::bytes, s>>>(a);
+    } else {
+        allow_max_dynamic_smem(prefill_attn_kernel<D, G, float>);
+        prefill_attn_kernel<D, G, float><<<grid, kPfThreads, PfLayout<D>::bytes, s>>>(a);
+    }
+    BC_LAUNCHED("prefill_attn_kernel");
+}
+
 // Decode attention over an f16 KV cache ------------------------------------------
 // One CTA (8 warps) per (sequence, KV head, split of the keys). The split's
 // key and value rows are staged in shared memory with 16-byte asynchronous
@@ -620,6 +805,29 @@ int plan_decode_splits(int batch, int kv_heads, int kv_len, int sm_count, int ma
 
 bool decode_attention_supported(int head_dim, int group) {
     return (head_dim == 64 || head_dim == 128) && (group == 1 || group == 2 || group == 4 || group == 8);
+}
+
+bool prefill_attention_supported(const AttnRowsArgs& a) {
+    const int64_t G = a.kv_heads > 0 ? a.heads / a.kv_heads : 0;
+    return a.batch == 1 && !a.mask && a.q_f16 == 0 && (a.d == 64 || a.d == 128) &&
+           (G == 1 || G == 2 || G == 4 || G == 8) && a.heads == G * a.kv_heads && a.q_ss % 4 == 0 &&
+           a.o_ss % 4 == 0 && a.o_sh % 4 == 0;
+}
+
+void launch_prefill_attention(const AttnRowsArgs& a, cudaStream_t s) {
+    if (a.sq == 0 || a.skv == 0) return;
+    if (!prefill_attention_supported(a)) invalid("prefill attention: unsupported layout");
+    const int G = (int)(a.heads / a.kv_heads);
+    if (a.d == 128) {
+        if (G == 8) return launch_prefill_t<128, 8>(a, s);
+        if (G == 4) return launch_prefill_t<128, 4>(a, s);
+        if (G == 2) return launch_prefill_t<128, 2>(a, s);
+        return launch_prefill_t<128, 1>(a, s);
+    }
+    if (G == 8) return launch_prefill_t<64, 8>(a, s);
+    if (G == 4) return launch_prefill_t<64, 4>(a, s);
+    if (G == 2) return launch_prefill_t<64, 2>(a, s);
+    return launch_prefill_t<64, 1>(a, s);
 }
 
 int decode_bulk_splits(int batch, int kv_heads, int sm_count) {

@@ -343,7 +343,12 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.o_sb = 0;
             a.o_sh = D;
             a.o_ss = m->qd;
-            launch_attention_rows(a, s);
+            // the tiled kernel in the fast numerics; the row kernel keeps the
+            // reference's summation order for the exact ones
+            if (gemv_mode(m) == MODE_FAST && prefill_attention_supported(a))
+                launch_prefill_attention(a, s);
+            else
+                launch_attention_rows(a, s);
         }
         // h = h + Wo attn ; under TP only rank 0 adds the residual, then sum
         const bool r0 = m->rank == 0;
@@ -911,7 +916,7 @@ int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* m, BeaconCudaStream* s
         require(m && stream && out_avg_us && out_bytes, "model_profile_linear: null argument");
         set_device(m->ctx);
         check_ready(m);
-        if (batch < 1 || batch > std::min(16, m->max_rows) || iters < 1) invalid("model_profile_linear: bad batch/iters");
+        if (batch < 1 || batch > m->max_rows || iters < 1) invalid("model_profile_linear: bad batch/iters");
         cudaStream_t s = stream->s;
         const int64_t hid = m->cfg.hidden_size;
         const QLayout* Lp;

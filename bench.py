@@ -410,22 +410,10 @@ def run_prefill(a):
     ttft_ms = e0.elapsed_time(e1) / steps
     value = NB * P / (ttft_ms / 1e3)
 
-    # GEMM roofline: gate/up (2F x H) at M = P rows
+    # GEMM roofline: the model's fused gate/up (2F x H) at M = P rows, every
+    # layer's weights in turn (L2-cold), through the model's own linear path
     H, F = shp["hidden_size"], shp["intermediate_size"]
-    st = be.new_stream()
-    w = be.quantize(st, be.upload((rng.standard_normal((2 * F, H), dtype=np.float32) * 0.02)), L.DTYPE_Q8_0)
-    x = be.upload(rng.standard_normal((P, H), dtype=np.float32))
-    gs = torch.cuda.ExternalStream(st.cuda_stream)
-    for _ in range(2):
-        be.quantized_matmul(st, x, w)
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 5
-    g0.record(gs)
-    for _ in range(reps):
-        be.quantized_matmul(st, x, w)
-    g1.record(gs)
-    g1.synchronize()
-    gemm_us = g0.elapsed_time(g1) * 1e3 / reps
+    gemm_us, _nb = model.profile_linear(L.W_GATE, P, 2)
     tflops = 2.0 * P * (2 * F) * H / (gemm_us * 1e-6) / 1e12
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:

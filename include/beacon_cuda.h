@@ -284,12 +284,14 @@ int32_t beacon_cuda_model_decode_step_device(BeaconCudaModel* model, BeaconCudaS
                                              const int32_t* d_tokens, int32_t batch,
                                              int32_t position, int32_t* d_next_tokens,
                                              float* d_logits);
-/* Times `iters` passes of one projection over every layer, using the decode
- * step's own kernels and buffers (each layer's weight is distinct, so reads
- * are L2-cold), with CUDA events on `stream`. slot: BEACON_CUDA_W_Q (the fused
- * q/k/v GEMV), _O, _GATE (the fused gate/up GEMV with SwiGLU), _DOWN or
- * _LM_HEAD. out_avg_us: mean duration of one launch; out_bytes: algorithmic
- * bytes of one launch (weight blocks + f32 activations in + f32 out). */
+/* Times `iters` passes of one projection over every layer, using the model's
+ * own kernels and buffers (each layer's weight is distinct, so reads are
+ * L2-cold), with CUDA events on `stream`. slot: BEACON_CUDA_W_Q (the fused
+ * q/k/v projection), _O, _GATE (the fused gate/up projection with SwiGLU),
+ * _DOWN or _LM_HEAD. batch: rows, up to the model's row capacity; more than
+ * 16 rows in the fast numerics run the prefill tensor-core GEMM. out_avg_us:
+ * mean duration of one launch; out_bytes: algorithmic bytes of one launch
+ * (weight blocks + f32 activations in + f32 out). */
 int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* model, BeaconCudaStream* stream, int32_t slot,
                                          int32_t batch, int32_t iters, float* out_avg_us,
                                          uint64_t* out_bytes);

@@ -233,3 +233,19 @@ def test_context_overflow_and_bad_tokens(be):
         m.decode_step([1], 8)
     with pytest.raises(ShapeMismatch):          # cpu_backend.rs:406-411
         m.forward([c["vocab_size"]], 0)
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_fast_prefill_long_prompt_tiled_attention(be, causal):
+    """A prompt longer than one 64-key tile and one 32-row query tile takes the
+    tiled prefill attention (fast numerics); logits stay within the bar of the
+    oracle, for the reference's unmasked prefill and for the causal one."""
+    from beacon_cuda import _lib as L
+    c = small_cfg(num_layers=2, max_context=200)
+    w = make_weights(oracle_cfg(c), orc.Q4_K, seed=81)
+    om = build_oracle_model(oracle_cfg(c, causal_prefill=causal), w)
+    m = cuda_model(be, c, w, numerics=L.NUMERICS_FAST, kv_dtype=L.DTYPE_F16, causal_prefill=causal)
+    prompt = list(np.random.default_rng(82 + causal).integers(0, c["vocab_size"], 150))
+    ref = om.forward(prompt, 0)
+    got = m.forward(prompt, 0)
+    assert np.abs(got - ref).max() <= LOGITS_TOL
