@@ -2,6 +2,7 @@
 // kernels: the tiled split-K kernel (gemv.cuh) and the persistent TMA-fed
 // stream-K kernel (gemv3.cuh).
 #include <algorithm>
+#include <cstdlib>
 
 #include "gemv3.cuh"
 #include "qgemm_tc.h"
@@ -77,7 +78,14 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     if (pairable) stages = (int)std::min<size_t>(stages, (half_sm - xb - 256) / (kG3Warps * tb));
     const int64_t total_tiles = L.groups() * L.ktiles();
     const int sms = ctx ? ctx->sm_count : 148;
-    const int cps = pairable && total_tiles >= (int64_t)sms * kG3Warps * 8 ? 2 : 1;
+    // BEACON_CUDA_GEMV_PAIR_TILES: tiles per warp from which two CTAs share an
+    // SM (default 1: 16 warps per SM measured fastest in the decode step; a
+    // large value keeps one CTA per SM everywhere)
+    static const int64_t pair_tiles = [] {
+        const char* e = std::getenv("BEACON_CUDA_GEMV_PAIR_TILES");
+        return e ? std::max<int64_t>(1, std::atoll(e)) : (int64_t)1;
+    }();
+    const int cps = pairable && total_tiles >= (int64_t)sms * kG3Warps * pair_tiles ? 2 : 1;
     const int64_t nctas = std::min<int64_t>((int64_t)sms * cps, total_tiles / kG3Warps);
     if (nctas < 1) return pl;
     if ((uint64_t)total_tiles * (uint64_t)(nctas * kG3Warps) >= (1ull << 32)) return pl;  // 32-bit tile arithmetic
