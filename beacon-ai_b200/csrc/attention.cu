@@ -697,27 +697,18 @@ __global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const 
     __syncthreads();
     if (!flag_s) return;
     // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-    // in split order. The partial sums of a round of 16 splits are requested
-    // first; the split weights are formed while they are in flight.
+    // in split order, 16 splits per round. The first round's partial sums and
+    // every split's m and l are requested together, so the common case (up to
+    // 16 splits) costs one round trip to L2.
+    static_assert(G <= kAttWarps, "one head per warp in the merge");
     const int ns = a.nsplit;
     float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][16]
     constexpr int OPT = (G * D + kAttThreads - 1) / kAttThreads;        // outputs per thread
-    float o[OPT];
+    float o[OPT], pa[OPT][16];
 #pragma unroll
     for (int t = 0; t < OPT; ++t) o[t] = 0.0f;
-    // M per head (every thread of a head's warp holds it)
-    for (int g = warp; g < G; g += kAttWarps) {
-        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
-        float M = -INFINITY;
-        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hb * ns + s2]));
-        M = warp_max(M);
-        if (lane == 0) m_s[g] = M;
-        if (lane == 0) l_s[g] = 0.0f;
-    }
-    __syncthreads();
-    for (int s0 = 0; s0 < ns; s0 += 16) {
+    auto load_round = [&](int s0) {
         const int nr = min(16, ns - s0);
-        float pa[OPT][16];
 #pragma unroll
         for (int t = 0; t < OPT; ++t) {
             const int i = tid + t * kAttThreads;
@@ -727,17 +718,46 @@ __global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const 
             for (int u = 0; u < 16; ++u)
                 pa[t][u] = (i < G * D && u < nr) ? __ldcg(&a.part_acc[(hb * ns + s0 + u) * D + dd]) : 0.0f;
         }
-        for (int g = warp; g < G; g += kAttWarps) {
-            const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+    };
+    load_round(0);
+    // warp g < G: head g. Lane j holds split j's m and l when there are at
+    // most 32 splits (else they are re-read per round).
+    const int64_t hbw = (int64_t)b * a.heads + kvh * G + (warp < G ? warp : 0);
+    float mreg = -INFINITY, lreg = 0.0f;
+    if (warp < G) {
+        if (lane < ns) {
+            mreg = __ldcg(&a.part_m[hbw * ns + lane]);
+            lreg = __ldcg(&a.part_l[hbw * ns + lane]);
+        }
+        float M = mreg;
+        for (int s2 = lane + 32; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hbw * ns + s2]));
+        M = warp_max(M);
+        if (lane == 0) {
+            m_s[warp] = M;
+            l_s[warp] = 0.0f;
+        }
+    }
+    __syncthreads();
+    for (int s0 = 0; s0 < ns; s0 += 16) {
+        const int nr = min(16, ns - s0);
+        if (s0 > 0) load_round(s0);
+        if (warp < G) {
+            float mm, ll;
+            if (ns <= 32) {
+                mm = __shfl_sync(0xffffffffu, mreg, (s0 + lane) & 31);
+                ll = __shfl_sync(0xffffffffu, lreg, (s0 + lane) & 31);
+            } else {
+                mm = lane < nr ? __ldcg(&a.part_m[hbw * ns + s0 + lane]) : -INFINITY;
+                ll = lane < nr ? __ldcg(&a.part_l[hbw * ns + s0 + lane]) : 0.0f;
+            }
             float w = 0.0f, lw = 0.0f;
             if (lane < nr) {
-                const float mm = __ldcg(&a.part_m[hb * ns + s0 + lane]);
-                w = mm == -INFINITY ? 0.0f : expf(mm - m_s[g]);
-                lw = __ldcg(&a.part_l[hb * ns + s0 + lane]) * w;
+                w = mm == -INFINITY ? 0.0f : expf(mm - m_s[warp]);
+                lw = ll * w;
             }
-            if (lane < 16) wts[g * 16 + lane] = w;
+            if (lane < 16) wts[warp * 16 + lane] = w;
             lw = warp_sum(lw);
-            if (lane == 0) l_s[g] += lw;
+            if (lane == 0) l_s[warp] += lw;
         }
         __syncthreads();
 #pragma unroll

@@ -53,7 +53,7 @@ METRIC = "decode tok/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=64)
+    p.add_argument("--steps", type=int, default=256)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=["auto"] + list(WORKLOADS), default="auto")
