@@ -444,7 +444,8 @@ def run_reference(a):
     batch = a.batch or WORKLOADS[wl]["batch"]
     sample = CpuDecodeSample(wl, batch)
     vals = []
-    for i in range(a.warmup + a.steps):
+    steps = min(a.steps, 32)  # each step is a bounded CPU sample; keep the run to a few minutes
+    for i in range(a.warmup + steps):
         tps, _ = sample.step()
         if i >= a.warmup:
             vals.append(tps)
