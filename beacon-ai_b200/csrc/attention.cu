@@ -14,6 +14,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "qx.cuh"
 
 namespace bc {
 
@@ -682,7 +683,10 @@ __global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const 
         for (int w = 0; w < kAttWarps; ++w) o += wacc[(w * G + g) * D + dd];
         const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
         if (a.nsplit == 1) {
-            a.out[hb * D + dd] = o * (1.0f / l_s[g]);
+            const float r = o * (1.0f / l_s[g]);
+            a.out[hb * D + dd] = r;
+            // a warp holds 32 consecutive dims of one head: one block of the o input
+            if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
         } else {
             a.part_acc[(hb * a.nsplit + split) * D + dd] = o;
             if (dd == 0) {
@@ -777,7 +781,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const 
         if (i >= G * D) continue;
         const int g = i / D, dd = i - g * D;
         const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
-        a.out[hb * D + dd] = o[t] * (1.0f / l_s[g]);
+        const float r = o[t] * (1.0f / l_s[g]);
+        a.out[hb * D + dd] = r;
+        if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
     }
     if (tid == 0) a.counters[bk] = 0;
 }

@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "kernels.h"
+
 namespace bc {
 
 // Strided exact attention, one CTA per query row. Element offsets:
@@ -53,6 +55,7 @@ struct DecodeAttnArgs {
     float* out;
     int* counters;  // [batch * kv_heads] arrival counters, zero at rest (f16 caches)
     int* err;       // set to 3 when a bounded wait gives up (f16 caches)
+    QxImage qy;     // f16 caches: also write the output quantised for the o projection
 };
 constexpr int kMaxDecodeSplits = 64;
 constexpr int kMaxBulkSplits = 256;

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "qx.cuh"
 
 namespace bc {
 
@@ -54,6 +55,8 @@ struct GemvParams {
     const float* norm_w;  // persistent kernel only: RMSNorm of each x row fused into the staging
     float norm_eps;
     QkvEpi qkv;           // EPI_QKV destinations
+    QxImage qx;           // pre-quantised activations (persistent kernel, FAST)
+    QxImage qy;           // EPI_ADD: y also written quantised for the next GEMV
 };
 
 __device__ __forceinline__ float load_x(const GemvParams& p, int b, int64_t kk) {
@@ -465,6 +468,21 @@ __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t
         }
         return;
     }
+    if (epi == EPI_ADD && p.qy.data) {
+        // also hand the next GEMV its quantised input (whole warp: shuffles)
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            if (b >= p.batch) break;
+            const bool ok = row < p.n;
+            float r = 0.0f;
+            if (ok) {
+                r = p.res[b * p.res_ld + row] + v[b];
+                p.y[b * p.y_ld + row] = r;
+            }
+            qx_write_group(p.qy, b, g, lane, r, ok);
+        }
+        return;
+    }
     if (row >= p.n) return;
 #pragma unroll
     for (int b = 0; b < B; ++b) {
@@ -577,6 +595,8 @@ void launch_qgemv_t(const GemvLaunch& a) {
     p.norm_w = nullptr;
     p.norm_eps = 0.0f;
     p.qkv = a.qkv ? *a.qkv : QkvEpi{};
+    p.qx = QxImage{};  // the tiled kernel stages its own activations
+    p.qy = a.qy;
     auto kern = qgemv_kernel<FMT, MODE, B>;
     if (pl.smem > 48 * 1024) allow_max_dynamic_smem(kern);
     const int64_t grid = a.L->groups() * pl.ksplit;

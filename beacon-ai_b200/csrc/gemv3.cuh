@@ -317,11 +317,45 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             mbar_expect_tx(&mybar[i], (uint32_t)tb);
             bulk_g2s(myring + (size_t)i * tb, p.w + (t_begin + i) * tb, (uint32_t)tb, &mybar[i]);
         }
+    __shared__ __align__(8) uint64_t qx_bar;
+    float inv[B];  // 1/rms per row when the producer quantised x * norm_w
+#pragma unroll
+    for (int b = 0; b < B; ++b) inv[b] = 1.0f;
+    const bool from_image = MODE == MODE_FAST && p.qx.data != nullptr;
     float4 nwr[kStageRegPasses];
-    prefetch_norm(p, a.kspan, nwr);
+    if (from_image) {
+        if (threadIdx.x == 0) {
+            mbar_init(&qx_bar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+    } else {
+        prefetch_norm(p, a.kspan, nwr);
+    }
     pdl_trigger();
     pdl_wait();
-    stage_x_full<FMT, MODE, B>(p, xs, a.kspan, nwr);
+    if (from_image) {
+        // the producer's staging image: bulk copies, and 1/rms from its block sums
+        __syncthreads();
+        const uint32_t bytes = (uint32_t)B * a.kspan * 2 + (uint32_t)B * (a.kspan / 32) * 8;  // the FAST image
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(&qx_bar, bytes);
+            for (uint32_t off = 0; off < bytes; off += 16384u)
+                bulk_g2s(xs + off, p.qx.data + off, min(16384u, bytes - off), &qx_bar);
+        }
+        if (p.qx.ss) {
+            const int nblk = a.kspan / 32;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                float t = 0.0f;
+                for (int j = lane; j < nblk; j += 32) t += __ldcg(&p.qx.ss[b * nblk + j]);
+                t = warp_sum(t);
+                inv[b] = 1.0f / sqrtf(t / (float)p.k + p.norm_eps);
+            }
+        }
+        if (!mbar_wait_bounded(&qx_bar, 0) && lane == 0) atomicExch(a.err, 1);
+    } else {
+        stage_x_full<FMT, MODE, B>(p, xs, a.kspan, nwr);
+    }
     __syncthreads();
 
     float acc[B];
@@ -362,6 +396,8 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
         if (t == KT - 1 || i == n - 1) {
             const uint32_t g0 = g * KT, g1 = g0 + KT;
             if (g0 >= tb0 && g1 <= te0) {
+#pragma unroll
+                for (int b = 0; b < B; ++b) acc[b] *= inv[b];
                 gemv_store<B>(p, epi, g, lane, acc);
             } else {
                 // contributors to group g: warps whose ranges meet [g0, g1)
@@ -403,6 +439,8 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
                                 for (int b = 0; b < B; ++b) v[b] += part[u][b];
                             }
                     }
+#pragma unroll
+                    for (int b = 0; b < B; ++b) v[b] *= inv[b];
                     gemv_store<B>(p, epi, g, lane, v);
                     if (lane == 0) a.counters[g] = 0;
                 }
@@ -453,6 +491,8 @@ void launch_qgemv3_t(const LinearPlan& pl, const GemvLaunch& a) {
     p.norm_w = a.norm_w;
     p.norm_eps = a.norm_eps;
     p.qkv = a.qkv ? *a.qkv : QkvEpi{};
+    p.qx = a.qx;
+    p.qy = a.qy;
     q.ktiles = a.L->ktiles();
     q.total_tiles = a.L->groups() * q.ktiles;
     q.total_warps = pl.total_warps;

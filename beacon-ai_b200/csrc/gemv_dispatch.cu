@@ -105,11 +105,21 @@ size_t LinearPlan::scratch_floats(int batch, const QLayout& L) const {
 void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
                    int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,
                    const GemvScratch& scratch, cudaStream_t s, const float* norm_w, float norm_eps, bool pdl,
-                   const QkvEpi* qkv) {
+                   const QkvEpi* qkv, const QxImage* qx, const QxImage* qy) {
     GemvLaunch a{&plan.v2, &L, w, x, x_f16, x_ld, batch, y, y_ld, epi, res, res_ld, mode, rtz, scratch, s};
     a.pdl = pdl;
     if (epi == EPI_QKV && !qkv) invalid("fused q/k/v epilogue launched without its destinations");
     a.qkv = qkv;
+    if (qx && qx->data) {
+        if (!plan.v3 || mode != MODE_FAST || qx->bpad != plan.bpad || qx->kspan != (int)L.k_pad)
+            invalid("pre-quantised activations need the persistent fast GEMV with the image's shape");
+        a.qx = *qx;
+    }
+    if (qy && qy->data) {
+        if (epi != EPI_ADD || qy->kspan < (int)L.n_pad || batch > qy->bpad)
+            invalid("quantised output needs the residual epilogue and an image covering the rows");
+        a.qy = *qy;
+    }
     if (!plan.v3) {
         if (norm_w) invalid("the tiled GEMV has no fused RMSNorm; normalise first");
         if (plan.v2.ksplit > 1 &&

@@ -21,6 +21,23 @@ enum GemvEpilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
 // Batch row b of the launch is model row row0 + b, at position
 // *pos_ptr (or pos_imm) + row * pos_step, in sequence row * seq_step; a
 // position outside [0, max_ctx) sets *err = 2 and writes nothing.
+// Activations quantised by the kernel that produces them (decode, fast
+// numerics): the consumer GEMV's shared-memory staging image, in global
+// memory -- int16 codes [bpad][kspan], f32 block scales [bpad][kspan/32],
+// int32 code sums [bpad][kspan/32] -- plus, when the consumer fuses an
+// RMSNorm, the sums of squares of the unnormalised values per 32-block
+// [bpad][kspan/32] (the codes are then of x * norm_w, and the consumer scales
+// its outputs by 1/rms). The producer writes rows b < batch only; rows
+// b >= batch stay as they were (the consumer never stores them).
+struct QxImage {
+    uint8_t* data = nullptr;         // staging image; null: none
+    float* ss = nullptr;             // per-block sums of squares; null: no norm
+    int kspan = 0;                   // consumer's padded K (multiple of 256)
+    int bpad = 1;                    // consumer's staged rows
+    int perm = 0;                    // 1: Q4_0 element order within 8-groups
+    const float* norm_w = nullptr;   // producer side: the consumer's norm weight
+};
+
 struct QkvEpi {
     float* q = nullptr;
     void* kc = nullptr;
@@ -85,6 +102,8 @@ struct GemvLaunch {
     float norm_eps = 0.0f;
     bool pdl = false;               // launch with programmatic stream serialisation
     const QkvEpi* qkv = nullptr;    // EPI_QKV destinations
+    QxImage qx;                     // consumer: pre-quantised activations (persistent kernel, FAST)
+    QxImage qy;                     // producer (EPI_ADD): also write y quantised for the next GEMV
 };
 
 // cudaLaunchKernelEx with programmatic stream serialisation when `pdl`.
@@ -134,7 +153,8 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
 void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
                    int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,
                    const GemvScratch& scratch, cudaStream_t s, const float* norm_w = nullptr, float norm_eps = 0.0f,
-                   bool pdl = false, const QkvEpi* qkv = nullptr);
+                   bool pdl = false, const QkvEpi* qkv = nullptr, const QxImage* qx = nullptr,
+                   const QxImage* qy = nullptr);
 void launch_qgemv3_q4_0(const LinearPlan& pl, const GemvLaunch& a);
 void launch_qgemv3_q8_0(const LinearPlan& pl, const GemvLaunch& a);
 void launch_qgemv3_q4_k(const LinearPlan& pl, const GemvLaunch& a);

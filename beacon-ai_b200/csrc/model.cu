@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "qx.cuh"
 #include "qgemm_tc.h"
 
 namespace bc {
@@ -39,19 +40,21 @@ constexpr int kPrefillChunk = 2048;
 // --- small kernels ------------------------------------------------------------
 
 // h[row] = E[tok[row]] (f32). Out-of-range ids write zeros and raise *err.
+// qy (hid % 32 == 0): also the first layer's quantised q/k/v input.
 __global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hid, const int32_t* tok, float* h,
-                             int* err) {
+                             int* err, QxImage qy) {
     pdl_trigger();
     pdl_wait();
     const int row = blockIdx.x;
     const int32_t t = tok[row];
     const bool ok = t >= 0 && t < vocab;
     if (!ok && threadIdx.x == 0) atomicExch(err, 1);
-    for (int64_t i = threadIdx.x; i < hid; i += blockDim.x) {
+    for (int64_t i = threadIdx.x; i < hid; i += blockDim.x) {  // warp-uniform when hid % 32 == 0
         float v = 0.0f;
         if (ok) v = e_f16 ? __half2float(static_cast<const __half*>(E)[(int64_t)t * hid + i])
                           : static_cast<const float*>(E)[(int64_t)t * hid + i];
         h[(int64_t)row * hid + i] = v;
+        if (qy.data) qx_write_group(qy, row, i >> 5, (int)(i & 31), v, true);
     }
 }
 
@@ -181,6 +184,13 @@ struct BeaconCudaModel {
     bc::GemvScratch gsc;
     std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
     std::unique_ptr<bc::DeviceBuffer> x16;  // f16 activations of the prefill GEMM
+    // decode hand-off of quantised activations between kernels (one GPU, fast
+    // numerics, batch <= 8): the hidden-state image (q/k/v, gate/up, lm_head
+    // inputs, with per-block sums of squares for their RMSNorm) and the
+    // attention-output image (o input)
+    std::unique_ptr<bc::DeviceBuffer> qx_buf;
+    uint8_t *qx_h = nullptr, *qx_a = nullptr;
+    float* qx_h_ss = nullptr;
     int attn_nsplit = 1;
     float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
     int* attn_cnt = nullptr;
@@ -203,10 +213,34 @@ int gemv_mode(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_
 bool gemv_rtz(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_NUMERICS_REF_RTZ; }
 
 // y = W x over `rows` rows of x, in chunks of 16 rows (the GEMV batch limit).
+// The quantised-activation hand-off applies to a decode step of the fast
+// numerics on one GPU whose consumers all run the persistent GEMV and whose
+// attention is the f16-cache kernel (the o input's producer).
+bool qx_active(const BeaconCudaModel* m, int rows, bool decode) {
+    if (!decode || !m->qx_buf || m->tp != 1 || gemv_mode(m) != MODE_FAST || rows > 8) return false;
+    if (m->cfg.kv_dtype != BEACON_CUDA_DTYPE_F16) return false;
+    for (const QLayout* L : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Llm})
+        if (!plan_linear(m->ctx, *L, rows, MODE_FAST).v3) return false;
+    return true;
+}
+
+// which: 0 the hidden-state image (norm_w: the consumer's RMSNorm weight), 1 the attention-output image
+QxImage qx_image(BeaconCudaModel* m, int which, const QLayout& consumer, int rows, const float* norm_w) {
+    QxImage q;
+    q.data = which ? m->qx_a : m->qx_h;
+    q.ss = which ? nullptr : m->qx_h_ss;
+    q.kspan = (int)consumer.k_pad;
+    q.bpad = plan_linear(m->ctx, consumer, rows, MODE_FAST).bpad;
+    q.perm = consumer.dtype == BEACON_CUDA_DTYPE_Q4_0 ? 1 : 0;
+    q.norm_w = norm_w;
+    return q;
+}
+
 // qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.
 // More than 16 rows in the fast numerics run as one tensor-core GEMM.
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
-            int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s, const QkvEpi* qkv = nullptr) {
+            int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s, const QkvEpi* qkv = nullptr,
+            const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
     if (rows > 16 && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L)) {
         QkvEpi qe;
         if (qkv) {
@@ -227,7 +261,7 @@ void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x,
         }
         launch_linear(pl, L, w, x + (int64_t)r0 * x_ld, false, x_ld, b, y + (int64_t)r0 * y_ld, y_ld, epi,
                       res ? res + (int64_t)r0 * res_ld : nullptr, res_ld, gemv_mode(m), gemv_rtz(m), m->gsc, s,
-                      nullptr, 0.0f, m->pdl, qkv ? &qe : nullptr);
+                      nullptr, 0.0f, m->pdl, qkv ? &qe : nullptr, r0 == 0 ? qx : nullptr, r0 == 0 ? qy : nullptr);
     }
 }
 
@@ -239,7 +273,8 @@ void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int
 // y = W rmsnorm(x, norm_w): the norm rides in the persistent GEMV's staging
 // when every row chunk takes that kernel, otherwise it runs on its own first.
 void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, const float* norm_w, int rows,
-                   float* y, int64_t y_ld, int epi, cudaStream_t s, const QkvEpi* qkv = nullptr) {
+                   float* y, int64_t y_ld, int epi, cudaStream_t s, const QkvEpi* qkv = nullptr,
+                   const QxImage* qx = nullptr) {
     const int64_t hid = m->cfg.hidden_size;
     bool fused = true;
     for (int r0 = 0; r0 < rows && fused; r0 += 16) fused = plan_linear(m->ctx, L, std::min(16, rows - r0), gemv_mode(m)).v3;
@@ -257,7 +292,8 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
             qe.row0 = r0;
         }
         launch_linear(pl, L, w, x + (int64_t)r0 * hid, false, hid, b, y + (int64_t)r0 * y_ld, y_ld, epi, nullptr, 0,
-                      gemv_mode(m), gemv_rtz(m), m->gsc, s, norm_w, m->cfg.rms_norm_eps, m->pdl, qkv ? &qe : nullptr);
+                      gemv_mode(m), gemv_rtz(m), m->gsc, s, norm_w, m->cfg.rms_norm_eps, m->pdl, qkv ? &qe : nullptr,
+                      r0 == 0 ? qx : nullptr);
     }
 }
 
@@ -270,8 +306,11 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
     const int D = c.head_dim;
     const bool f16kv = c.kv_dtype == BEACON_CUDA_DTYPE_F16;
     const int64_t cache_sb = (int64_t)c.max_context * m->kd;
+    const bool qxa = qx_active(m, rows, decode);
     for (int li = 0; li < c.num_layers; ++li) {
         LayerW& L = m->layers[li];
+        const float* attn_nw = static_cast<const float*>(L.attn_norm->ptr);
+        const float* ffn_nw = static_cast<const float*>(L.ffn_norm->ptr);
         {
             // q/k/v projection with RoPE and the KV cache write in its epilogue
             QkvEpi qe;
@@ -291,8 +330,9 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             qe.seq_step = decode ? 1 : 0;
             qe.max_ctx = (int)c.max_context;
             qe.err = m->err_dev;
-            normed_linear(m, m->Lqkv, L.wqkv->ptr, m->h, static_cast<const float*>(L.attn_norm->ptr), rows, m->qkv,
-                          m->qkv_n, EPI_QKV, s, &qe);
+            const QxImage in = qxa ? qx_image(m, 0, m->Lqkv, rows, attn_nw) : QxImage{};
+            normed_linear(m, m->Lqkv, L.wqkv->ptr, m->h, attn_nw, rows, m->qkv, m->qkv_n, EPI_QKV, s, &qe,
+                          qxa ? &in : nullptr);
         }
         const float scale = 1.0f / sqrtf((float)D);  // engine.rs:415
         if (decode) {
@@ -317,6 +357,7 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.part_m = m->pm;
             a.part_l = m->pl;
             a.out = m->attn;
+            if (qxa) a.qy = qx_image(m, 1, m->Lo, rows, nullptr);
             launch_decode_attention(a, s, m->pdl);
         } else {
             AttnRowsArgs a{};
@@ -352,18 +393,36 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
         }
         // h = h + Wo attn ; under TP only rank 0 adds the residual, then sum
         const bool r0 = m->rank == 0;
-        linear(m, m->Lo, L.wo->ptr, m->attn, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE, r0 ? m->h : nullptr,
-               hid, s);
+        {
+            const QxImage in = qxa ? qx_image(m, 1, m->Lo, rows, nullptr) : QxImage{};
+            const QxImage out = qxa ? qx_image(m, 0, m->Lgu, rows, ffn_nw) : QxImage{};
+            linear(m, m->Lo, L.wo->ptr, m->attn, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE,
+                   r0 ? m->h : nullptr, hid, s, nullptr, qxa ? &in : nullptr, qxa ? &out : nullptr);
+        }
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
-        normed_linear(m, m->Lgu, L.wgu->ptr, m->h, static_cast<const float*>(L.ffn_norm->ptr), rows, m->ffn, m->f_loc,
-                      EPI_SWIGLU, s);
-        linear(m, m->Ld, L.wd->ptr, m->ffn, m->f_loc, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE, r0 ? m->h : nullptr,
-               hid, s);
+        {
+            const QxImage in = qxa ? qx_image(m, 0, m->Lgu, rows, ffn_nw) : QxImage{};
+            normed_linear(m, m->Lgu, L.wgu->ptr, m->h, ffn_nw, rows, m->ffn, m->f_loc, EPI_SWIGLU, s, nullptr,
+                          qxa ? &in : nullptr);
+        }
+        {
+            // the next consumer of h: the next layer's q/k/v, or the lm_head after the last layer
+            const bool last = li + 1 == c.num_layers;
+            const float* next_nw = last ? static_cast<const float*>(m->final_norm->ptr)
+                                        : static_cast<const float*>(m->layers[li + 1].attn_norm->ptr);
+            const QxImage out = qxa ? qx_image(m, 0, last ? m->Llm : m->Lqkv, rows, next_nw) : QxImage{};
+            linear(m, m->Ld, L.wd->ptr, m->ffn, m->f_loc, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE,
+                   r0 ? m->h : nullptr, hid, s, nullptr, nullptr, qxa ? &out : nullptr);
+        }
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
     }
     // final norm + lm_head (engine.rs:230-234)
-    normed_linear(m, m->Llm, m->wlm->ptr, m->h, static_cast<const float*>(m->final_norm->ptr), rows, m->logits_loc,
-                  m->v_loc, EPI_STORE, s);
+    {
+        const float* fnw = static_cast<const float*>(m->final_norm->ptr);
+        const QxImage in = qxa ? qx_image(m, 0, m->Llm, rows, fnw) : QxImage{};
+        normed_linear(m, m->Llm, m->wlm->ptr, m->h, fnw, rows, m->logits_loc, m->v_loc, EPI_STORE, s, nullptr,
+                      qxa ? &in : nullptr);
+    }
     if (m->tp > 1) {
         comm_all_gather(m->ctx, m->logits_loc, m->logits_all, (size_t)rows * m->v_loc, s);
     }
@@ -381,9 +440,12 @@ void finish_logits(BeaconCudaModel* m, int rows, bool need_full_logits, bool fee
 float* full_logits(BeaconCudaModel* m) { return m->tp > 1 ? m->logits : m->logits_loc; }
 
 void decode_body(BeaconCudaModel* m, int batch, bool autoregressive, cudaStream_t s) {
+    const QxImage qy = qx_active(m, batch, true)
+                           ? qx_image(m, 0, m->Lqkv, batch, static_cast<const float*>(m->layers[0].attn_norm->ptr))
+                           : QxImage{};
     launch_kernel(embed_kernel, dim3(batch), dim3(256), 0, s, m->pdl, (const void*)m->embed->ptr,
                   (int)(m->embed_dtype == BEACON_CUDA_DTYPE_F16), (int64_t)m->cfg.vocab_size,
-                  (int64_t)m->cfg.hidden_size, (const int32_t*)m->tok, m->h, m->err_dev);
+                  (int64_t)m->cfg.hidden_size, (const int32_t*)m->tok, m->h, m->err_dev, qy);
     run_layers(m, batch, true, m->pos_dev, 0, s);
     finish_logits(m, batch, m->tp > 1, autoregressive, s);
     if (autoregressive) launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, m->pdl, m->pos_dev);
@@ -583,6 +645,17 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
         m->pl = m->pm + pa;
         m->attn_cnt = reinterpret_cast<int*>(m->pl + pa);
         BC_CUDA(cudaMemset(m->attn_cnt, 0, ncnt * 4));
+        if (tp == 1 && c.hidden_size % 32 == 0) {
+            const int64_t kh = (c.hidden_size + 255) / 256 * 256, ka = (m->qd + 255) / 256 * 256;
+            auto image_bytes = [](int64_t kspan) { return (size_t)8 * kspan * 2 + (size_t)8 * (kspan / 32) * 8; };
+            const size_t img_h = image_bytes(kh), img_a = image_bytes(ka);
+            const size_t ss_bytes = (size_t)8 * (kh / 32) * 4;
+            m->qx_buf = std::make_unique<DeviceBuffer>(img_h + img_a + ss_bytes);
+            BC_CUDA(cudaMemset(m->qx_buf->ptr, 0, img_h + img_a + ss_bytes));
+            m->qx_h = static_cast<uint8_t*>(m->qx_buf->ptr);
+            m->qx_a = m->qx_h + img_h;
+            m->qx_h_ss = reinterpret_cast<float*>(m->qx_a + img_a);
+        }
         const size_t na = argmax_scratch_count(m->v_loc, tp, (int)R);
         m->argmax_buf = std::make_unique<DeviceBuffer>(na * sizeof(ArgmaxSummary));
         m->argmax_scratch = static_cast<ArgmaxSummary*>(m->argmax_buf->ptr);
@@ -795,7 +868,7 @@ int32_t beacon_cuda_model_forward(BeaconCudaModel* m, BeaconCudaStream* stream, 
             for (int i = 0; i < rows; ++i) m->h_stage[i] = (int32_t)tokens[t0 + i];
             BC_CUDA(cudaMemcpyAsync(m->tok, m->h_stage, (size_t)rows * 4, cudaMemcpyHostToDevice, s));
             embed_kernel<<<rows, 256, 0, s>>>(m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, V, c.hidden_size,
-                                              m->tok, m->h, m->err_dev);
+                                              m->tok, m->h, m->err_dev, QxImage{});
             BC_LAUNCHED("embed_kernel");
             run_layers(m, rows, false, nullptr, position + t0, s);
             finish_logits(m, rows, true, false, s);
