@@ -1,0 +1,351 @@
+// attn_unit.cuh -- one unit of split-K decode attention over an f16 KV cache
+// on a whole CTA, shared by the decode attention kernel (attention.cu) and the
+// fused decode step (decode_mega.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "attention.h"
+#include "common.cuh"
+#include "qx.cuh"
+
+namespace bc {
+
+// Decode attention over an f16 KV cache ------------------------------------------
+// One CTA (8 warps) per (sequence, KV head, split of the keys). The split's
+// key and value rows are staged in shared memory with 16-byte asynchronous
+// copies, 64 keys per stage in a ring of up to 4 stages whose completion is
+// tracked by one mbarrier per stage. Every row except the decoded token's
+// (written by the previous kernel) is requested before the kernel waits on its
+// predecessor, so the cache stream overlaps the preceding GEMV.
+// Scores: lane l holds head dims [l*DPL, l*DPL+DPL) of all G query heads in
+// registers; a warp takes 32/G keys at a time and a transposing butterfly
+// (31 shuffles) leaves lane l with the full dot product of (key l/G, head
+// l%G). Values: lanes over head dims, warps over keys, with an online softmax
+// across stages (engine.rs:415-440). The splits of a (sequence, KV head) are
+// merged in split order by the last of its CTAs to finish (arrival counter),
+// so no separate combine kernel runs.
+constexpr int kAttKeys = 64;
+constexpr int kAttStages = 4;
+constexpr int kAttThreads = 256;
+constexpr int kAttWarps = kAttThreads / 32;
+
+template <int D>
+struct AttLayout {
+    static constexpr int row = 2 * D;                      // bytes of one key or value row
+    static constexpr int stage = 2 * kAttKeys * row;       // keys, then values
+    static constexpr int chunks = 2 * kAttKeys * row / 16;  // 16-byte copies per stage
+    static constexpr size_t smem = (size_t)kAttStages * stage;
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// The barrier receives one arrival from this thread once all of its earlier
+// asynchronous copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One (sequence, KV head, split) unit on the whole CTA (kAttThreads threads):
+// ring = ST stages of staged K/V rows, bars = ST mbarriers (initialised here).
+// wait() separates the requests that depend on nothing in flight from the
+// rest (the kernel's wait on its predecessor, or a grid barrier).
+template <int D, int G, int ST, typename Wait>
+__device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int split, uint8_t* att_smem,
+                                          uint64_t* bars, Wait wait) {
+    using Lay = AttLayout<D>;
+    constexpr int kAttStages = ST;
+    constexpr int DPL = D / 32;   // head dims per lane
+    constexpr int KB = 32 / G;    // keys per score batch
+    constexpr int NB = kAttKeys / KB;  // score batches per stage
+    __shared__ __align__(16) float ps[kAttKeys][G];
+    __shared__ float corr_s[G], m_s[G], l_s[G];
+    __shared__ int flag_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int b = bk / a.kv_heads, kvh = bk - b * a.kv_heads;
+    // the key range: the position counter is not written during a step
+    const int kv_len = max(1, min(a.max_kv, a.pos_ptr ? *a.pos_ptr + 1 : a.kv_len));
+    const int chunk = (kv_len + a.nsplit - 1) / a.nsplit;
+    const int k0 = min(kv_len, split * chunk), k1 = min(kv_len, k0 + chunk);
+    const int nkeys = k1 - k0;
+    const int nsteps = (nkeys + kAttKeys - 1) / kAttKeys;
+    const int cur = kv_len - 1;  // the decoded token's row
+    const int cur_step = (cur >= k0 && cur < k1) ? (cur - k0) / kAttKeys : -1;
+    const int64_t ks = (int64_t)a.kv_heads * D;
+    const __half* kc = reinterpret_cast<const __half*>(a.k_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    const __half* vc = reinterpret_cast<const __half*>(a.v_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    // 16-byte chunk c of a stage: row c / (D/8) (keys, then values), part c % (D/8)
+    constexpr int CPR = D / 8;
+    auto issue = [&](int s, bool skip_cur) {
+        uint8_t* base = att_smem + (size_t)(s % kAttStages) * Lay::stage;
+        for (int c = tid; c < Lay::chunks; c += kAttThreads) {
+            const int row = c / CPR, part = c - row * CPR;
+            const int r = row & (kAttKeys - 1);
+            const int key = k0 + s * kAttKeys + r;
+            if (key >= k1 || (skip_cur && key == cur)) continue;
+            const __half* src = (row < kAttKeys ? kc : vc) + key * ks + part * 8;
+            cp_async16(base + row * Lay::row + part * 16, src);
+        }
+    };
+    const int npre = min(kAttStages, nsteps);
+    if (tid == 0) {
+        for (int s = 0; s < kAttStages; ++s) mbar_init(&bars[s], kAttThreads);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    for (int s = 0; s < npre; ++s) {
+        issue(s, true);
+        // the decoded token's rows come after the wait: their copiers arrive then
+        if (s != cur_step || tid >= 2 * CPR) cp_async_arrive(&bars[s]);
+    }
+    wait();
+    if (cur_step >= 0 && cur_step < npre && tid < 2 * CPR) {
+        uint8_t* base = att_smem + (size_t)cur_step * Lay::stage;
+        const int r = cur - k0 - cur_step * kAttKeys;
+        const int row = tid < CPR ? r : kAttKeys + r, part = tid < CPR ? tid : tid - CPR;
+        cp_async16(base + row * Lay::row + part * 16, (tid < CPR ? kc : vc) + cur * ks + part * 8);
+        cp_async_arrive(&bars[cur_step]);
+    }
+    // this lane's head dims of the G queries, pre-scaled
+    float qr[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j)
+            qr[g][j] = a.q[((int64_t)b * a.heads + kvh * G + g) * D + lane * DPL + j] * a.scale;
+    if (tid < G) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.0f;
+    }
+    float acc[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[g][j] = 0.0f;
+    __syncthreads();
+    int s = 0;
+    bool failed = false;
+    for (; s < nsteps; ++s) {
+        const int st = s % kAttStages;
+        const bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((s / kAttStages) & 1));
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        const int n = min(kAttKeys, k1 - (k0 + s * kAttKeys));
+        const uint8_t* kbase = att_smem + (size_t)st * Lay::stage;
+        const uint8_t* vbase = kbase + kAttKeys * Lay::row;
+        // scores: batches of KB keys, transposed across the warp
+        for (int bt = warp; bt < NB; bt += kAttWarps) {
+            float v[32];
+#pragma unroll
+            for (int kk = 0; kk < KB; ++kk) {
+                const __half* kr = reinterpret_cast<const __half*>(kbase + (bt * KB + kk) * Lay::row) + lane * DPL;
+                float kf[DPL];
+#pragma unroll
+                for (int j = 0; j < DPL; j += 2) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(kr + j));
+                    kf[j] = f.x;
+                    kf[j + 1] = f.y;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float t = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < DPL; ++j) t = fmaf(qr[g][j], kf[j], t);
+                    v[kk * G + g] = t;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const bool upper = (lane & o) != 0;
+#pragma unroll
+                for (int i = 0; i < o; ++i) {
+                    const float send = upper ? v[i] : v[i + o];
+                    const float keep = upper ? v[i + o] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            const int key = bt * KB + lane / G;
+            ps[key][lane % G] = key < n ? v[0] : -INFINITY;
+        }
+        __syncthreads();
+        // online softmax bookkeeping: warp w keeps heads w, w + 8, ...
+        for (int g = warp; g < G; g += kAttWarps) {
+            const float s0 = ps[lane][g], s1 = ps[lane + 32][g];
+            const float mo = m_s[g];
+            const float mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
+            const float c = mo == -INFINITY ? 0.0f : expf(mo - mn);
+            const float p0 = lane < n ? expf(s0 - mn) : 0.0f;
+            const float p1 = lane + 32 < n ? expf(s1 - mn) : 0.0f;
+            ps[lane][g] = p0;
+            ps[lane + 32][g] = p1;
+            const float sum = warp_sum(p0 + p1);
+            if (lane == 0) {
+                l_s[g] = l_s[g] * c + sum;
+                m_s[g] = mn;
+                corr_s[g] = c;
+            }
+        }
+        __syncthreads();
+        // values: warp w takes keys w, w + 8, ... of the stage
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float c = corr_s[g];
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[g][j] *= c;
+        }
+#pragma unroll 2
+        for (int r = warp; r < n; r += kAttWarps) {
+            const __half* vr = reinterpret_cast<const __half*>(vbase + r * Lay::row) + lane * DPL;
+            float vf[DPL];
+#pragma unroll
+            for (int j = 0; j < DPL; j += 2) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr + j));
+                vf[j] = f.x;
+                vf[j + 1] = f.y;
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float p = ps[r][g];
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) acc[g][j] = fmaf(p, vf[j], acc[g][j]);
+            }
+        }
+        __syncthreads();  // stage st is free again
+        if (s + kAttStages < nsteps) {
+            issue(s + kAttStages, false);
+            cp_async_arrive(&bars[st]);
+        }
+    }
+    if (failed) {
+        // let the copies still in flight land before the CTA exits
+        for (int s2 = s; s2 < nsteps && s2 < s + kAttStages; ++s2)
+            mbar_wait_bounded(&bars[s2 % kAttStages], (uint32_t)((s2 / kAttStages) & 1));
+        if (tid == 0) atomicExch(a.err, 3);
+        return;
+    }
+    // merge the warps (the ring is idle now)
+    float* wacc = reinterpret_cast<float*>(att_smem);  // [warps][G][D]
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) wacc[(warp * G + g) * D + lane * DPL + j] = acc[g][j];
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kAttThreads) {
+        const int g = i / D, dd = i - g * D;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttWarps; ++w) o += wacc[(w * G + g) * D + dd];
+        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+        if (a.nsplit == 1) {
+            const float r = o * (1.0f / l_s[g]);
+            a.out[hb * D + dd] = r;
+            // a warp holds 32 consecutive dims of one head: one block of the o input
+            if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
+        } else {
+            a.part_acc[(hb * a.nsplit + split) * D + dd] = o;
+            if (dd == 0) {
+                a.part_m[hb * a.nsplit + split] = m_s[g];
+                a.part_l[hb * a.nsplit + split] = l_s[g];
+            }
+        }
+    }
+    if (a.nsplit == 1) return;
+    __syncthreads();  // every partial store precedes thread 0's release
+    if (tid == 0) flag_s = atomic_add_acq_rel_gpu(&a.counters[bk], 1) == a.nsplit - 1;
+    __syncthreads();
+    if (!flag_s) return;
+    // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+    // in split order, 16 splits per round. The first round's partial sums and
+    // every split's m and l are requested together, so the common case (up to
+    // 16 splits) costs one round trip to L2.
+    static_assert(G <= kAttWarps, "one head per warp in the merge");
+    const int ns = a.nsplit;
+    float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][16]
+    constexpr int OPT = (G * D + kAttThreads - 1) / kAttThreads;        // outputs per thread
+    float o[OPT], pa[OPT][16];
+#pragma unroll
+    for (int t = 0; t < OPT; ++t) o[t] = 0.0f;
+    auto load_round = [&](int s0) {
+        const int nr = min(16, ns - s0);
+#pragma unroll
+        for (int t = 0; t < OPT; ++t) {
+            const int i = tid + t * kAttThreads;
+            const int g = i / D, dd = i - g * D;
+            const int64_t hb = (int64_t)b * a.heads + kvh * G + (g < G ? g : 0);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                pa[t][u] = (i < G * D && u < nr) ? __ldcg(&a.part_acc[(hb * ns + s0 + u) * D + dd]) : 0.0f;
+        }
+    };
+    load_round(0);
+    // warp g < G: head g. Lane j holds split j's m and l when there are at
+    // most 32 splits (else they are re-read per round).
+    const int64_t hbw = (int64_t)b * a.heads + kvh * G + (warp < G ? warp : 0);
+    float mreg = -INFINITY, lreg = 0.0f;
+    if (warp < G) {
+        if (lane < ns) {
+            mreg = __ldcg(&a.part_m[hbw * ns + lane]);
+            lreg = __ldcg(&a.part_l[hbw * ns + lane]);
+        }
+        float M = mreg;
+        for (int s2 = lane + 32; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hbw * ns + s2]));
+        M = warp_max(M);
+        if (lane == 0) {
+            m_s[warp] = M;
+            l_s[warp] = 0.0f;
+        }
+    }
+    __syncthreads();
+    for (int s0 = 0; s0 < ns; s0 += 16) {
+        const int nr = min(16, ns - s0);
+        if (s0 > 0) load_round(s0);
+        if (warp < G) {
+            float mm, ll;
+            if (ns <= 32) {
+                mm = __shfl_sync(0xffffffffu, mreg, (s0 + lane) & 31);
+                ll = __shfl_sync(0xffffffffu, lreg, (s0 + lane) & 31);
+            } else {
+                mm = lane < nr ? __ldcg(&a.part_m[hbw * ns + s0 + lane]) : -INFINITY;
+                ll = lane < nr ? __ldcg(&a.part_l[hbw * ns + s0 + lane]) : 0.0f;
+            }
+            float w = 0.0f, lw = 0.0f;
+            if (lane < nr) {
+                w = mm == -INFINITY ? 0.0f : expf(mm - m_s[warp]);
+                lw = ll * w;
+            }
+            if (lane < 16) wts[warp * 16 + lane] = w;
+            lw = warp_sum(lw);
+            if (lane == 0) l_s[warp] += lw;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < OPT; ++t) {
+            const int i = tid + t * kAttThreads;
+            const int g = i / D;
+            if (i < G * D)
+#pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    if (u < nr) o[t] = fmaf(pa[t][u], wts[g * 16 + u], o[t]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int t = 0; t < OPT; ++t) {
+        const int i = tid + t * kAttThreads;
+        if (i >= G * D) continue;
+        const int g = i / D, dd = i - g * D;
+        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+        const float r = o[t] * (1.0f / l_s[g]);
+        a.out[hb * D + dd] = r;
+        if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
+    }
+    if (tid == 0) a.counters[bk] = 0;
+}
+
+}  // namespace bc

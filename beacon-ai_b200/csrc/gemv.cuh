@@ -410,6 +410,31 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
 }
 
 // Epilogue --------------------------------------------------------------------
+// The SwiGLU outputs of row groups 2j and 2j+1 form the 32-element block j of
+// the next GEMV's input: the second of the two groups to finish (an
+// acquire/release arrival counter per pair) reads both halves back and writes
+// the block into the consumer's staging image. Whole warp.
+template <int B>
+__device__ __forceinline__ void swiglu_handoff(const GemvParams& p, int64_t g, int lane) {
+    const int64_t j = g >> 1;
+    int second = 1;  // a last group without a partner writes its block alone
+    if ((g | 1) < p.n_pad / 32) {
+        __syncwarp();
+        if (lane == 0) second = atomic_add_acq_rel_gpu(&p.qy.pairs[j], 1) == 1;
+        second = __shfl_sync(0xffffffffu, second, 0);
+        if (!second) return;
+        if (lane == 0) p.qy.pairs[j] = 0;
+    }
+    const int64_t fe = j * 32 + lane;
+    const bool valid = 2 * fe < p.n;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        if (b >= p.batch) break;
+        const float x = valid ? __ldcg(&p.y[b * p.y_ld + fe]) : 0.0f;
+        qx_write_group(p.qy, b, j, lane, x, valid);
+    }
+}
+
 template <int B>
 __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t g, int lane,
                                            const float (&v)[B]) {
@@ -466,6 +491,7 @@ __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t
                 p.y[b * p.y_ld + f] = (gte * sig) * up;
             }
         }
+        if (p.qy.data) swiglu_handoff<B>(p, g, lane);
         return;
     }
     if (epi == EPI_ADD && p.qy.data) {

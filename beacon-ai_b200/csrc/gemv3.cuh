@@ -287,11 +287,96 @@ __device__ __forceinline__ void stage_x_full(const GemvParams& p, uint8_t* xs, i
     }
 }
 
+// One tile of a warp's stream, read from its ring slot (lane = row).
+template <int FMT>
+struct G3Tile {
+    uint4 meta;
+    uint4 q[Fmt<FMT>::CH];
+};
+
+template <int FMT>
+__device__ __forceinline__ void g3_load_tile(const uint8_t* tp, int lane, G3Tile<FMT>& r) {
+    r.meta = reinterpret_cast<const uint4*>(tp)[lane];
+#pragma unroll
+    for (int c = 0; c < Fmt<FMT>::CH; ++c) r.q[c] = reinterpret_cast<const uint4*>(tp + 512 + c * 512)[lane];
+}
+
+template <int FMT, int MODE, int B>
+__device__ __forceinline__ void g3_consume_tile(const G3Tile<FMT>& r, const uint8_t* xs, int kspan, int t,
+                                                float (&acc)[B], bool rtz) {
+    if (FMT == FMT_Q4_0)
+        consume_q4_0<MODE, B>(r.meta, *reinterpret_cast<const uint4(*)[8]>(r.q), xs, kspan, t, acc, rtz);
+    else if (FMT == FMT_Q8_0)
+        consume_q8_0<MODE, B>(r.meta, *reinterpret_cast<const uint4(*)[16]>(r.q), xs, kspan, t, acc, rtz);
+    else
+        consume_q4_k<MODE, B>(r.meta, *reinterpret_cast<const uint4(*)[8]>(r.q), xs, kspan, t, acc, rtz);
+}
+
+// End of row group g in warp gw's range [tb0, te0): store it if the warp owns
+// all of it, else publish the partial and let the group's last contributor
+// (acquire/release arrival counter) sum the contributors in warp order and
+// store. Whole warp. acc is scaled by inv (1/rms rows) before the epilogue.
+template <int B>
+__device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t T, uint32_t W,
+                                                uint32_t KT, uint32_t tb0, uint32_t te0, int64_t gw, int lane,
+                                                float (&acc)[B], const float (&inv)[B]) {
+    const GemvParams& p = a.p;
+    const uint32_t g0 = g * KT, g1 = g0 + KT;
+    if (g0 >= tb0 && g1 <= te0) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] *= inv[b];
+        gemv_store<B>(p, epi, g, lane, acc);
+        return;
+    }
+    // contributors to group g: warps whose ranges meet [g0, g1)
+    const uint32_t wf = ((g0 + 1) * W - 1) / T;
+    const uint32_t wl = (g1 * W - 1) / T;
+    const int slot = (tb0 >= g0) ? 0 : 1;  // 0: g is the first group of my range
+    float* mine = a.slots + ((gw * 2 + slot) * B) * 32;
+#pragma unroll
+    for (int b = 0; b < B; ++b) __stcg(&mine[b * 32 + lane], acc[b]);
+    // __syncwarp orders the lanes' stores before lane 0's release;
+    // the last arriver's acquire makes every contributor's visible
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomic_add_acq_rel_gpu(&a.counters[g], 1) == (int)(wl - wf);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    if (!last) return;
+    constexpr int U = B >= 8 ? 1 : 8 / B;  // contributor slots loaded together
+    float v[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) v[b] = 0.0f;
+    for (uint32_t w0 = wf; w0 <= wl; w0 += U) {
+        float part[U][B];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint32_t w2 = w0 + u;
+            if (w2 <= wl) {
+                const uint32_t s2 = w2 * T / W;
+                const int sl = (s2 >= g0) ? 0 : 1;  // g is w2's first group iff its range starts in g
+                const float* src = a.slots + (((int64_t)w2 * 2 + sl) * B) * 32;
+#pragma unroll
+                for (int b = 0; b < B; ++b) part[u][b] = __ldcg(&src[b * 32 + lane]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (w0 + u <= wl) {
+#pragma unroll
+                for (int b = 0; b < B; ++b) v[b] += part[u][b];
+            }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) v[b] *= inv[b];
+    gemv_store<B>(p, epi, g, lane, v);
+    if (lane == 0) a.counters[g] = 0;
+}
+
 template <int FMT, int MODE, int B>
 __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel(const Gemv3Params a, const int epi) {
     extern __shared__ __align__(128) uint8_t g3_smem[];
     uint8_t* smem = g3_smem;
-    constexpr int CH = Fmt<FMT>::CH;
     const GemvParams& p = a.p;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.stages;
@@ -375,76 +460,18 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             ok = false;
             break;
         }
-        const uint8_t* tp = myring + (size_t)st * tb;
-        const uint4 meta = reinterpret_cast<const uint4*>(tp)[lane];
-        uint4 q[CH];
-#pragma unroll
-        for (int c = 0; c < CH; ++c) q[c] = reinterpret_cast<const uint4*>(tp + 512 + c * 512)[lane];
+        G3Tile<FMT> tile;
+        g3_load_tile<FMT>(myring + (size_t)st * tb, lane, tile);
         __syncwarp();
         if (lane == 0 && i + S < n) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_expect_tx(&mybar[st], (uint32_t)tb);
             bulk_g2s(myring + (size_t)st * tb, p.w + (t_begin + i + S) * tb, (uint32_t)tb, &mybar[st]);
         }
-        if (FMT == FMT_Q4_0)
-            consume_q4_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), xs, a.kspan, (int)t, acc, rtz);
-        else if (FMT == FMT_Q8_0)
-            consume_q8_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[16]>(q), xs, a.kspan, (int)t, acc, rtz);
-        else
-            consume_q4_k<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), xs, a.kspan, (int)t, acc, rtz);
+        g3_consume_tile<FMT, MODE, B>(tile, xs, a.kspan, (int)t, acc, rtz);
         // end of a row group (or of this warp's range): finish it
         if (t == KT - 1 || i == n - 1) {
-            const uint32_t g0 = g * KT, g1 = g0 + KT;
-            if (g0 >= tb0 && g1 <= te0) {
-#pragma unroll
-                for (int b = 0; b < B; ++b) acc[b] *= inv[b];
-                gemv_store<B>(p, epi, g, lane, acc);
-            } else {
-                // contributors to group g: warps whose ranges meet [g0, g1)
-                const uint32_t wf = ((g0 + 1) * W - 1) / T;
-                const uint32_t wl = (g1 * W - 1) / T;
-                const int slot = (tb0 >= g0) ? 0 : 1;  // 0: g is the first group of my range
-                float* mine = a.slots + ((gw * 2 + slot) * B) * 32;
-#pragma unroll
-                for (int b = 0; b < B; ++b) __stcg(&mine[b * 32 + lane], acc[b]);
-                // __syncwarp orders the lanes' stores before lane 0's release;
-                // the last arriver's acquire makes every contributor's visible
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) last = atomic_add_acq_rel_gpu(&a.counters[g], 1) == (int)(wl - wf);
-                last = __shfl_sync(0xffffffffu, last, 0);
-                __syncwarp();
-                if (last) {
-                    constexpr int U = B >= 8 ? 1 : 8 / B;  // contributor slots loaded together
-                    float v[B];
-#pragma unroll
-                    for (int b = 0; b < B; ++b) v[b] = 0.0f;
-                    for (uint32_t w0 = wf; w0 <= wl; w0 += U) {
-                        float part[U][B];
-#pragma unroll
-                        for (int u = 0; u < U; ++u) {
-                            const uint32_t w2 = w0 + u;
-                            if (w2 <= wl) {
-                                const uint32_t s2 = w2 * T / W;
-                                const int sl = (s2 >= g0) ? 0 : 1;  // g is w2's first group iff its range starts in g
-                                const float* src = a.slots + (((int64_t)w2 * 2 + sl) * B) * 32;
-#pragma unroll
-                                for (int b = 0; b < B; ++b) part[u][b] = __ldcg(&src[b * 32 + lane]);
-                            }
-                        }
-#pragma unroll
-                        for (int u = 0; u < U; ++u)
-                            if (w0 + u <= wl) {
-#pragma unroll
-                                for (int b = 0; b < B; ++b) v[b] += part[u][b];
-                            }
-                    }
-#pragma unroll
-                    for (int b = 0; b < B; ++b) v[b] *= inv[b];
-                    gemv_store<B>(p, epi, g, lane, v);
-                    if (lane == 0) a.counters[g] = 0;
-                }
-            }
+            g3_finish_group<B>(a, epi, g, T, W, KT, tb0, te0, gw, lane, acc, inv);
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = 0.0f;
         }

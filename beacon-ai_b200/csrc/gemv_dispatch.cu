@@ -116,9 +116,20 @@ void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, cons
         a.qx = *qx;
     }
     if (qy && qy->data) {
-        if (epi != EPI_ADD || qy->kspan < (int)L.n_pad || batch > qy->bpad)
-            invalid("quantised output needs the residual epilogue and an image covering the rows");
+        if (!plan.v3 || mode != MODE_FAST || batch > qy->bpad)
+            invalid("quantised output needs the persistent fast GEMV and an image covering the batch");
+        if (epi == EPI_ADD) {
+            if (qy->kspan < (int)L.n_pad) invalid("quantised output: the image is narrower than the rows");
+        } else if (epi == EPI_SWIGLU) {
+            if (qy->kspan < (int)(L.n_pad / 2) || qy->norm_w || qy->ss)
+                invalid("quantised SwiGLU output: the image must cover n/2 columns, without a norm");
+            if (!scratch.counters || scratch.counter_count < L.groups() + (L.groups() + 1) / 2)
+                invalid("quantised SwiGLU output launched without its pair counters");
+        } else {
+            invalid("quantised output needs the residual or SwiGLU epilogue");
+        }
         a.qy = *qy;
+        if (epi == EPI_SWIGLU) a.qy.pairs = scratch.counters + L.groups();
     }
     if (!plan.v3) {
         if (norm_w) invalid("the tiled GEMV has no fused RMSNorm; normalise first");

@@ -36,6 +36,7 @@ struct QxImage {
     int bpad = 1;                    // consumer's staged rows
     int perm = 0;                    // 1: Q4_0 element order within 8-groups
     const float* norm_w = nullptr;   // producer side: the consumer's norm weight
+    int* pairs = nullptr;            // SwiGLU producer: one arrival counter per two 16-output groups (zero at rest)
 };
 
 struct QkvEpi {

@@ -189,7 +189,7 @@ struct BeaconCudaModel {
     // inputs, with per-block sums of squares for their RMSNorm) and the
     // attention-output image (o input)
     std::unique_ptr<bc::DeviceBuffer> qx_buf;
-    uint8_t *qx_h = nullptr, *qx_a = nullptr;
+    uint8_t *qx_h = nullptr, *qx_a = nullptr, *qx_f = nullptr;
     float* qx_h_ss = nullptr;
     int attn_nsplit = 1;
     float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
@@ -219,16 +219,17 @@ bool gemv_rtz(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_
 bool qx_active(const BeaconCudaModel* m, int rows, bool decode) {
     if (!decode || !m->qx_buf || m->tp != 1 || gemv_mode(m) != MODE_FAST || rows > 8) return false;
     if (m->cfg.kv_dtype != BEACON_CUDA_DTYPE_F16) return false;
-    for (const QLayout* L : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Llm})
+    for (const QLayout* L : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Ld, &m->Llm})
         if (!plan_linear(m->ctx, *L, rows, MODE_FAST).v3) return false;
     return true;
 }
 
-// which: 0 the hidden-state image (norm_w: the consumer's RMSNorm weight), 1 the attention-output image
+// which: 0 the hidden-state image (norm_w: the consumer's RMSNorm weight), 1 the attention-output image,
+// 2 the SwiGLU-output image (the down projection's input)
 QxImage qx_image(BeaconCudaModel* m, int which, const QLayout& consumer, int rows, const float* norm_w) {
     QxImage q;
-    q.data = which ? m->qx_a : m->qx_h;
-    q.ss = which ? nullptr : m->qx_h_ss;
+    q.data = which == 0 ? m->qx_h : which == 1 ? m->qx_a : m->qx_f;
+    q.ss = which == 0 ? m->qx_h_ss : nullptr;
     q.kspan = (int)consumer.k_pad;
     q.bpad = plan_linear(m->ctx, consumer, rows, MODE_FAST).bpad;
     q.perm = consumer.dtype == BEACON_CUDA_DTYPE_Q4_0 ? 1 : 0;
@@ -274,7 +275,7 @@ void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int
 // when every row chunk takes that kernel, otherwise it runs on its own first.
 void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, const float* norm_w, int rows,
                    float* y, int64_t y_ld, int epi, cudaStream_t s, const QkvEpi* qkv = nullptr,
-                   const QxImage* qx = nullptr) {
+                   const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
     const int64_t hid = m->cfg.hidden_size;
     bool fused = true;
     for (int r0 = 0; r0 < rows && fused; r0 += 16) fused = plan_linear(m->ctx, L, std::min(16, rows - r0), gemv_mode(m)).v3;
@@ -293,7 +294,7 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
         }
         launch_linear(pl, L, w, x + (int64_t)r0 * hid, false, hid, b, y + (int64_t)r0 * y_ld, y_ld, epi, nullptr, 0,
                       gemv_mode(m), gemv_rtz(m), m->gsc, s, norm_w, m->cfg.rms_norm_eps, m->pdl, qkv ? &qe : nullptr,
-                      r0 == 0 ? qx : nullptr);
+                      r0 == 0 ? qx : nullptr, r0 == 0 ? qy : nullptr);
     }
 }
 
@@ -402,17 +403,19 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
         {
             const QxImage in = qxa ? qx_image(m, 0, m->Lgu, rows, ffn_nw) : QxImage{};
+            const QxImage out = qxa ? qx_image(m, 2, m->Ld, rows, nullptr) : QxImage{};
             normed_linear(m, m->Lgu, L.wgu->ptr, m->h, ffn_nw, rows, m->ffn, m->f_loc, EPI_SWIGLU, s, nullptr,
-                          qxa ? &in : nullptr);
+                          qxa ? &in : nullptr, qxa ? &out : nullptr);
         }
         {
             // the next consumer of h: the next layer's q/k/v, or the lm_head after the last layer
             const bool last = li + 1 == c.num_layers;
             const float* next_nw = last ? static_cast<const float*>(m->final_norm->ptr)
                                         : static_cast<const float*>(m->layers[li + 1].attn_norm->ptr);
+            const QxImage in = qxa ? qx_image(m, 2, m->Ld, rows, nullptr) : QxImage{};
             const QxImage out = qxa ? qx_image(m, 0, last ? m->Llm : m->Lqkv, rows, next_nw) : QxImage{};
             linear(m, m->Ld, L.wd->ptr, m->ffn, m->f_loc, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE,
-                   r0 ? m->h : nullptr, hid, s, nullptr, nullptr, qxa ? &out : nullptr);
+                   r0 ? m->h : nullptr, hid, s, nullptr, qxa ? &in : nullptr, qxa ? &out : nullptr);
         }
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
     }
@@ -646,15 +649,18 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
         m->attn_cnt = reinterpret_cast<int*>(m->pl + pa);
         BC_CUDA(cudaMemset(m->attn_cnt, 0, ncnt * 4));
         if (tp == 1 && c.hidden_size % 32 == 0) {
-            const int64_t kh = (c.hidden_size + 255) / 256 * 256, ka = (m->qd + 255) / 256 * 256;
+            const int64_t kh = (c.hidden_size + 255) / 256 * 256, ka = (m->qd + 255) / 256 * 256,
+                          kf = (m->f_loc + 255) / 256 * 256;  // the down projection's k_pad
             auto image_bytes = [](int64_t kspan) { return (size_t)8 * kspan * 2 + (size_t)8 * (kspan / 32) * 8; };
-            const size_t img_h = image_bytes(kh), img_a = image_bytes(ka);
+            const size_t img_h = image_bytes(kh), img_a = image_bytes(ka), img_f = image_bytes(kf);
             const size_t ss_bytes = (size_t)8 * (kh / 32) * 4;
-            m->qx_buf = std::make_unique<DeviceBuffer>(img_h + img_a + ss_bytes);
-            BC_CUDA(cudaMemset(m->qx_buf->ptr, 0, img_h + img_a + ss_bytes));
+            const size_t total = img_h + img_a + img_f + ss_bytes;
+            m->qx_buf = std::make_unique<DeviceBuffer>(total);
+            BC_CUDA(cudaMemset(m->qx_buf->ptr, 0, total));
             m->qx_h = static_cast<uint8_t*>(m->qx_buf->ptr);
             m->qx_a = m->qx_h + img_h;
-            m->qx_h_ss = reinterpret_cast<float*>(m->qx_a + img_a);
+            m->qx_f = m->qx_a + img_a;
+            m->qx_h_ss = reinterpret_cast<float*>(m->qx_f + img_f);
         }
         const size_t na = argmax_scratch_count(m->v_loc, tp, (int)R);
         m->argmax_buf = std::make_unique<DeviceBuffer>(na * sizeof(ArgmaxSummary));
@@ -802,7 +808,8 @@ int32_t beacon_cuda_model_set_weight(BeaconCudaModel* m, int32_t layer, int32_t 
                 LinearPlan pl = plan_linear(m->ctx, *Lp, b, gemv_mode(m));
                 need_p = std::max(need_p, pl.scratch_floats(b, *Lp));
             }
-            need_c = std::max(need_c, Lp->groups());
+            // gate/up adds one SwiGLU hand-off counter per two row groups
+            need_c = std::max(need_c, Lp->groups() + (Lp == &m->Lgu ? (Lp->groups() + 1) / 2 : 0));
         }
         if (need_p > m->gsc.partial_floats || need_c > m->gsc.counter_count || !m->gsc.err) {
             const size_t pf = std::max(need_p, m->gsc.partial_floats), cc = (size_t)std::max(need_c, m->gsc.counter_count);
