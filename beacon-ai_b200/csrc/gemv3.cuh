@@ -4,15 +4,20 @@
 //  * persistent CTAs (one per SM) of 8 warps; the activations are staged once
 //    per CTA, for all K, with an optional fused RMSNorm of each row
 //    (ops.rs:77-93) so the norm needs no kernel of its own;
-//  * stream-K over tiles: the row-group tiles form one contiguous array, and
-//    warp w of W streams tiles [w*T/W, (w+1)*T/W), so every warp reads the
-//    same number of bytes (+-1 tile) whatever N and K are;
+//  * stream-K over tiles: the row-group tiles form one contiguous array; CTA
+//    c of C takes tiles [c*T/C, (c+1)*T/C) and its warp w the w-th eighth of
+//    that range, so every warp reads the same number of bytes (+-1 tile)
+//    whatever N and K are. When there are no more row groups than CTA slots
+//    (and a group has at least 8 tiles) each CTA takes exactly one group;
 //  * each warp owns a ring of S tile buffers in shared memory filled by 1-D
 //    bulk asynchronous copies (cp.async.bulk, completion on an mbarrier) that
 //    lane 0 issues S tiles ahead, across row-group boundaries too;
 //  * a row group wholly inside one warp's range is finished by that warp; a
-//    group cut by a range boundary is summed by its last contributor in warp
-//    order (fixed order, so results are deterministic);
+//    group cut by warp ranges is summed in two levels: the warps of a CTA
+//    through shared memory (the last of them to arrive sums in warp order),
+//    then, for a group cut by a CTA range boundary, the CTAs through global
+//    slots (the last CTA to arrive sums in CTA order); fixed orders, so
+//    results are deterministic;
 //  * programmatic dependent launch: the first S tiles of every warp are
 //    requested before waiting on the previous kernel (weights are never
 //    written), so the weight stream overlaps the previous kernel's tail.
@@ -26,6 +31,7 @@
 namespace bc {
 
 constexpr int kG3Warps = 8;
+constexpr int kG3MaxCtaGroups = 64;  // row groups one CTA range may touch (shared arrival counters)
 
 struct Gemv3Params {
     GemvParams p;         // w, n, n_pad, x, x_f16, x_ld, k, batch, y, y_ld, res, res_ld, rtz, norm_w
@@ -34,7 +40,7 @@ struct Gemv3Params {
     int64_t total_warps;
     int stages;
     int kspan;            // staged activation columns (k_pad)
-    float* slots;         // [total_warps][2][B][32] partial sums
+    float* slots;         // [CTAs][2][B][32] partial sums of the CTAs' first and last groups
     int* counters;        // [groups], zero at rest
     int* err;             // set to 1 when a wait gives up
 };
@@ -312,57 +318,103 @@ __device__ __forceinline__ void g3_consume_tile(const G3Tile<FMT>& r, const uint
         consume_q4_k<MODE, B>(r.meta, *reinterpret_cast<const uint4(*)[8]>(r.q), xs, kspan, t, acc, rtz);
 }
 
-// End of row group g in warp gw's range [tb0, te0): store it if the warp owns
-// all of it, else publish the partial and let the group's last contributor
-// (acquire/release arrival counter) sum the contributors in warp order and
-// store. Whole warp. acc is scaled by inv (1/rms rows) before the epilogue.
+// Bytes of the staged activations (FAST: int16 codes, then per 32-column
+// block a float scale and an int code sum; F32: floats), 16-byte multiple.
+template <int MODE, int B>
+__host__ __device__ __forceinline__ size_t g3_x_bytes(int kspan) {
+    return MODE == MODE_F32 ? (size_t)B * kspan * 4 : (size_t)B * kspan * 2 + (size_t)B * (kspan / 32) * 8;
+}
+inline size_t gemv3_red_bytes(int bpad) { return (size_t)kG3Warps * 2 * bpad * 32 * 4; }
+
+// Tile ranges of one warp: the grid's T tiles over C CTAs, the CTA's n
+// tiles [cb, ce) over its 8 warps; this warp (w) holds [wb, we).
+struct G3Range {
+    uint32_t T, C, c, cb, ce, n, w, wb, we;
+};
+
+// End of row group g in this warp's range: store it if the warp holds all of
+// it; else leave the warp's partial in shared memory, and the last warp of
+// the CTA to arrive sums the CTA's share of g in warp order; if other CTAs
+// hold part of g that sum goes to the CTA's global slot and the last CTA to
+// arrive (acquire/release arrival counter) sums the slots in CTA order and
+// stores. Whole warp. The sum is scaled by inv (1/rms rows) before the
+// epilogue. red: [8 warps][2][B][32] floats; cnt: the CTA's arrival counters.
 template <int B>
-__device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t T, uint32_t W,
-                                                uint32_t KT, uint32_t tb0, uint32_t te0, int64_t gw, int lane,
-                                                float (&acc)[B], const float (&inv)[B]) {
+__device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t KT,
+                                                const G3Range& r, int lane, float (&acc)[B],
+                                                const float (&inv)[B], float* red, int* cnt) {
     const GemvParams& p = a.p;
     const uint32_t g0 = g * KT, g1 = g0 + KT;
-    if (g0 >= tb0 && g1 <= te0) {
+    float v[B];
+    if (g0 >= r.wb && g1 <= r.we) {
 #pragma unroll
-        for (int b = 0; b < B; ++b) acc[b] *= inv[b];
-        gemv_store<B>(p, epi, g, lane, acc);
+        for (int b = 0; b < B; ++b) v[b] = acc[b] * inv[b];
+        gemv_store<B>(p, epi, g, lane, v);
         return;
     }
-    // contributors to group g: warps whose ranges meet [g0, g1)
-    const uint32_t wf = ((g0 + 1) * W - 1) / T;
-    const uint32_t wl = (g1 * W - 1) / T;
-    const int slot = (tb0 >= g0) ? 0 : 1;  // 0: g is the first group of my range
-    float* mine = a.slots + ((gw * 2 + slot) * B) * 32;
+    // level 1: the CTA's warps holding part of g, [wf, wl]
+    const uint32_t lo = max(g0, r.cb) - r.cb, hi = min(g1, r.ce) - r.cb;
+    const uint32_t wf = ((lo + 1) * kG3Warps - 1) / r.n, wl = (hi * kG3Warps - 1) / r.n;
 #pragma unroll
-    for (int b = 0; b < B; ++b) __stcg(&mine[b * 32 + lane], acc[b]);
+    for (int b = 0; b < B; ++b) v[b] = acc[b];
+    if (wf < wl) {
+        float* mine = red + ((r.w * 2 + (r.wb >= g0 ? 0 : 1)) * B) * 32;
+#pragma unroll
+        for (int b = 0; b < B; ++b) mine[b * 32 + lane] = acc[b];
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&cnt[g - r.cb / KT], 1) == (int)(wl - wf);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        __threadfence_block();
+#pragma unroll
+        for (int b = 0; b < B; ++b) v[b] = 0.0f;
+        for (uint32_t w2 = wf; w2 <= wl; ++w2) {
+            const uint32_t s2 = r.cb + w2 * r.n / kG3Warps;  // g is w2's first group iff its range starts in g
+            const float* src = red + ((w2 * 2 + (s2 >= g0 ? 0 : 1)) * B) * 32;
+#pragma unroll
+            for (int b = 0; b < B; ++b) v[b] += src[b * 32 + lane];
+        }
+    }
+    if (g0 >= r.cb && g1 <= r.ce) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) v[b] *= inv[b];
+        gemv_store<B>(p, epi, g, lane, v);
+        return;
+    }
+    // level 2: the CTAs holding part of g, [cf, cl]
+    const uint32_t cf = ((g0 + 1) * r.C - 1) / r.T, cl = (g1 * r.C - 1) / r.T;
+    float* mine = a.slots + (((int64_t)r.c * 2 + (r.cb >= g0 ? 0 : 1)) * B) * 32;
+#pragma unroll
+    for (int b = 0; b < B; ++b) __stcg(&mine[b * 32 + lane], v[b]);
     // __syncwarp orders the lanes' stores before lane 0's release;
     // the last arriver's acquire makes every contributor's visible
     __syncwarp();
     int last = 0;
-    if (lane == 0) last = atomic_add_acq_rel_gpu(&a.counters[g], 1) == (int)(wl - wf);
+    if (lane == 0) last = atomic_add_acq_rel_gpu(&a.counters[g], 1) == (int)(cl - cf);
     last = __shfl_sync(0xffffffffu, last, 0);
     __syncwarp();
     if (!last) return;
     constexpr int U = B >= 8 ? 1 : 8 / B;  // contributor slots loaded together
-    float v[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) v[b] = 0.0f;
-    for (uint32_t w0 = wf; w0 <= wl; w0 += U) {
+    for (uint32_t c0 = cf; c0 <= cl; c0 += U) {
         float part[U][B];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const uint32_t w2 = w0 + u;
-            if (w2 <= wl) {
-                const uint32_t s2 = w2 * T / W;
-                const int sl = (s2 >= g0) ? 0 : 1;  // g is w2's first group iff its range starts in g
-                const float* src = a.slots + (((int64_t)w2 * 2 + sl) * B) * 32;
+            const uint32_t c2 = c0 + u;
+            if (c2 <= cl) {
+                const uint32_t s2 = (uint32_t)((uint64_t)c2 * r.T / r.C);
+                const int sl = (s2 >= g0) ? 0 : 1;  // g is c2's first group iff its range starts in g
+                const float* src = a.slots + (((int64_t)c2 * 2 + sl) * B) * 32;
 #pragma unroll
                 for (int b = 0; b < B; ++b) part[u][b] = __ldcg(&src[b * 32 + lane]);
             }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u)
-            if (w0 + u <= wl) {
+            if (c0 + u <= cl) {
 #pragma unroll
                 for (int b = 0; b < B; ++b) v[b] += part[u][b];
             }
@@ -384,13 +436,25 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                       // [warps][S]
     uint8_t* ring = smem + 128 * ((kG3Warps * S * 8 + 127) / 128);           // [warps][S][tile]
     uint8_t* xs = ring + (size_t)kG3Warps * S * tb;                          // staged activations
+    float* red = reinterpret_cast<float*>(xs + g3_x_bytes<MODE, B>(a.kspan));  // [warps][2][B][32] partials
     uint64_t* mybar = bars + warp * S;
     uint8_t* myring = ring + (size_t)warp * S * tb;
 
-    const int64_t gw = (int64_t)blockIdx.x * kG3Warps + warp;
-    const int64_t t_begin = gw * a.total_tiles / a.total_warps;
-    const int64_t t_end = (gw + 1) * a.total_tiles / a.total_warps;
-    const int n = (int)(t_end - t_begin);
+    // 32-bit tile arithmetic (the host keeps total_tiles * CTAs < 2^32)
+    G3Range rg;
+    rg.T = (uint32_t)a.total_tiles;
+    rg.C = gridDim.x;
+    rg.c = blockIdx.x;
+    rg.cb = rg.c * rg.T / rg.C;
+    rg.ce = (rg.c + 1) * rg.T / rg.C;
+    rg.n = rg.ce - rg.cb;
+    rg.w = (uint32_t)warp;
+    rg.wb = rg.cb + rg.w * rg.n / kG3Warps;
+    rg.we = rg.cb + (rg.w + 1) * rg.n / kG3Warps;
+    const int64_t t_begin = rg.wb;
+    const int n = (int)(rg.we - rg.wb);
+    __shared__ int cta_cnt[kG3MaxCtaGroups];  // arrivals per row group of this CTA's range
+    for (int i = threadIdx.x; i < kG3MaxCtaGroups; i += blockDim.x) cta_cnt[i] = 0;
 
     if (lane == 0)
         for (int s = 0; s < S; ++s) mbar_init(&mybar[s], 1);
@@ -448,11 +512,9 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     for (int b = 0; b < B; ++b) acc[b] = 0.0f;
     const bool rtz = p.rtz != 0;
     bool ok = true;
-    // 32-bit tile arithmetic (the host keeps total_tiles * total_warps < 2^32)
-    const uint32_t T = (uint32_t)a.total_tiles, W = (uint32_t)a.total_warps, KT = (uint32_t)a.ktiles;
-    const uint32_t tb0 = (uint32_t)t_begin, te0 = (uint32_t)t_end;
-    uint32_t g = tb0 / KT;        // row group of the current tile
-    uint32_t t = tb0 - g * KT;    // its k-tile
+    const uint32_t KT = (uint32_t)a.ktiles;
+    uint32_t g = rg.wb / KT;      // row group of the current tile
+    uint32_t t = rg.wb - g * KT;  // its k-tile
     int i = 0;
     for (; i < n; ++i) {
         const int st = i % S;
@@ -471,7 +533,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
         g3_consume_tile<FMT, MODE, B>(tile, xs, a.kspan, (int)t, acc, rtz);
         // end of a row group (or of this warp's range): finish it
         if (t == KT - 1 || i == n - 1) {
-            g3_finish_group<B>(a, epi, g, T, W, KT, tb0, te0, gw, lane, acc, inv);
+            g3_finish_group<B>(a, epi, g, KT, rg, lane, acc, inv, red, cta_cnt);
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = 0.0f;
         }

@@ -56,7 +56,9 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
 // an SM: the ring is then sized to keep a CTA under half the SM's shared
 // memory, which lets the next kernel's CTA start (and fetch its weights)
 // while this one finishes, and GEMVs with many tiles per warp run two CTAs
-// per SM for more warps in flight.
+// per SM for more warps in flight. A GEMV with no more row groups than CTA
+// slots (and at least 8 k-tiles) runs one CTA per row group, whose warps
+// split the group's K and sum in shared memory: no cross-CTA exchange.
 int device_smem_optin() {
     int dev = 0, v = 0;
     cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
@@ -70,7 +72,7 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     if (batch > 8) return pl;
     pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : 8;
     const size_t budget = 200 * 1024, half_sm = 110 * 1024;
-    const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad);
+    const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad);
     const size_t tb = (size_t)L.tile_bytes;
     if (xb + 256 + 2 * kG3Warps * tb > budget) return pl;
     int stages = (int)std::min<size_t>(6, (budget - xb - 256) / (kG3Warps * tb));
@@ -86,9 +88,18 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
         return e ? std::max<int64_t>(1, std::atoll(e)) : (int64_t)1;
     }();
     const int cps = pairable && total_tiles >= (int64_t)sms * kG3Warps * pair_tiles ? 2 : 1;
-    const int64_t nctas = std::min<int64_t>((int64_t)sms * cps, total_tiles / kG3Warps);
+    // BEACON_CUDA_GEMV_WHOLE_GROUPS=0: stream-K even where one CTA per row
+    // group fits (default: one CTA per group, reduced in shared memory only)
+    static const bool whole_ok = [] {
+        const char* e = std::getenv("BEACON_CUDA_GEMV_WHOLE_GROUPS");
+        return !(e && std::atoi(e) == 0);
+    }();
+    const bool whole = whole_ok && L.ktiles() >= kG3Warps && L.groups() <= (int64_t)sms * cps;
+    const int64_t nctas = whole ? L.groups() : std::min<int64_t>((int64_t)sms * cps, total_tiles / kG3Warps);
     if (nctas < 1) return pl;
-    if ((uint64_t)total_tiles * (uint64_t)(nctas * kG3Warps) >= (1ull << 32)) return pl;  // 32-bit tile arithmetic
+    if ((uint64_t)total_tiles * (uint64_t)nctas >= (1ull << 32)) return pl;  // 32-bit tile arithmetic
+    const int64_t per_cta = (total_tiles + nctas - 1) / nctas;
+    if (per_cta / L.ktiles() + 2 > kG3MaxCtaGroups) return pl;  // the CTA's arrival counters
     pl.v3 = true;
     pl.stages = stages;
     pl.nctas = (int)nctas;
@@ -98,7 +109,7 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
 }
 
 size_t LinearPlan::scratch_floats(int batch, const QLayout& L) const {
-    if (v3) return (size_t)total_warps * 2 * bpad * 32;
+    if (v3) return (size_t)nctas * 2 * bpad * 32;
     return v2.ksplit > 1 ? (size_t)v2.ksplit * batch * L.n_pad : 0;
 }
 
