@@ -261,25 +261,27 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
     __syncthreads();
     if (!flag_s) return;
     // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-    // in split order, 16 splits per round. The first round's partial sums and
+    // in split order, MR splits per round (32 while a thread's share of the
+    // round fits in 64 registers, else 16). The first round's partial sums and
     // every split's m and l are requested together, so the common case (up to
-    // 16 splits) costs one round trip to L2.
+    // MR splits) costs one round trip to L2.
     static_assert(G <= kAttWarps, "one head per warp in the merge");
     const int ns = a.nsplit;
-    float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][16]
     constexpr int OPT = (G * D + kAttThreads - 1) / kAttThreads;        // outputs per thread
-    float o[OPT], pa[OPT][16];
+    constexpr int MR = OPT <= 2 ? 32 : 16;                              // splits per round
+    float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][MR]
+    float o[OPT], pa[OPT][MR];
 #pragma unroll
     for (int t = 0; t < OPT; ++t) o[t] = 0.0f;
     auto load_round = [&](int s0) {
-        const int nr = min(16, ns - s0);
+        const int nr = min(MR, ns - s0);
 #pragma unroll
         for (int t = 0; t < OPT; ++t) {
             const int i = tid + t * kAttThreads;
             const int g = i / D, dd = i - g * D;
             const int64_t hb = (int64_t)b * a.heads + kvh * G + (g < G ? g : 0);
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
+            for (int u = 0; u < MR; ++u)
                 pa[t][u] = (i < G * D && u < nr) ? __ldcg(&a.part_acc[(hb * ns + s0 + u) * D + dd]) : 0.0f;
         }
     };
@@ -302,8 +304,8 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
         }
     }
     __syncthreads();
-    for (int s0 = 0; s0 < ns; s0 += 16) {
-        const int nr = min(16, ns - s0);
+    for (int s0 = 0; s0 < ns; s0 += MR) {
+        const int nr = min(MR, ns - s0);
         if (s0 > 0) load_round(s0);
         if (warp < G) {
             float mm, ll;
@@ -319,7 +321,7 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
                 w = mm == -INFINITY ? 0.0f : expf(mm - m_s[warp]);
                 lw = ll * w;
             }
-            if (lane < 16) wts[warp * 16 + lane] = w;
+            if (lane < MR) wts[warp * MR + lane] = w;
             lw = warp_sum(lw);
             if (lane == 0) l_s[warp] += lw;
         }
@@ -330,8 +332,8 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
             const int g = i / D;
             if (i < G * D)
 #pragma unroll
-                for (int u = 0; u < 16; ++u)
-                    if (u < nr) o[t] = fmaf(pa[t][u], wts[g * 16 + u], o[t]);
+                for (int u = 0; u < MR; ++u)
+                    if (u < nr) o[t] = fmaf(pa[t][u], wts[g * MR + u], o[t]);
         }
         __syncthreads();
     }

@@ -57,14 +57,19 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
 // memory, which lets the next kernel's CTA start (and fetch its weights)
 // while this one finishes, and GEMVs with many tiles per warp run two CTAs
 // per SM for more warps in flight. A GEMV with no more row groups than CTA
-// slots (and at least 8 k-tiles) runs one CTA per row group, whose warps
-// split the group's K and sum in shared memory: no cross-CTA exchange.
+// slots, whose groups have 8 to 8 * stages k-tiles, runs one CTA per row
+// group, whose warps split the group's K and sum in shared memory: no
+// cross-CTA exchange.
 int device_smem_optin() {
     int dev = 0, v = 0;
     cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
     cuda_check(cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev), "cudaDeviceGetAttribute");
     return v;
 }
+
+// Dynamic shared memory that keeps a CTA alone on its SM (two need more than
+// the SM's 228 KB) but leaves room for a half-SM CTA of another kernel.
+constexpr size_t kSpreadSmem = 117 * 1024;
 
 LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
     LinearPlan pl;
@@ -94,7 +99,10 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
         const char* e = std::getenv("BEACON_CUDA_GEMV_WHOLE_GROUPS");
         return !(e && std::atoi(e) == 0);
     }();
-    const bool whole = whole_ok && L.ktiles() >= kG3Warps && L.groups() <= (int64_t)sms * cps;
+    // one CTA per row group when the groups fit the SM slots and a group's
+    // tiles fit its CTA's ring (all of its weights are requested at launch)
+    const bool whole = whole_ok && L.ktiles() >= kG3Warps && L.ktiles() <= (int64_t)kG3Warps * stages &&
+                       L.groups() <= (int64_t)sms * (pairable ? 2 : 1);
     const int64_t nctas = whole ? L.groups() : std::min<int64_t>((int64_t)sms * cps, total_tiles / kG3Warps);
     if (nctas < 1) return pl;
     if ((uint64_t)total_tiles * (uint64_t)nctas >= (1ull << 32)) return pl;  // 32-bit tile arithmetic
@@ -105,6 +113,10 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     pl.nctas = (int)nctas;
     pl.total_warps = nctas * kG3Warps;
     pl.smem = gemv3_bar_bytes(stages) + (size_t)kG3Warps * stages * tb + xb;
+    // no more CTAs than SMs: ask for more than half an SM's shared memory so
+    // the block scheduler cannot put two on one SM (it packs CTAs that fit,
+    // leaving SMs idle), while one CTA of the next kernel still fits beside
+    if (nctas <= sms && pairable) pl.smem = std::max<size_t>(pl.smem, kSpreadSmem);
     return pl;
 }
 
