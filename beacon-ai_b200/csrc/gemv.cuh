@@ -435,10 +435,20 @@ __device__ __forceinline__ void swiglu_handoff(const GemvParams& p, int64_t g, i
     }
 }
 
+// Epilogue operands of one row group loaded ahead of its finish (lane = row):
+// the residual rows and the next GEMV's norm weight.
+template <int B>
+struct EpiPre {
+    int64_t g = -1;  // the group they belong to; -1: none
+    float res[B];
+    float nw;
+};
+
 template <int B>
 __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t g, int lane,
-                                           const float (&v)[B]) {
+                                           const float (&v)[B], const EpiPre<B>* pre = nullptr) {
     const int64_t row = g * 32 + lane;
+    const bool have = pre && pre->g == g;
     if (epi == EPI_QKV) {
         // the whole warp takes part: pairs (2i, 2i+1) are lanes (l, l ^ 1)
         const QkvEpi& e = p.qkv;
@@ -502,10 +512,10 @@ __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t
             const bool ok = row < p.n;
             float r = 0.0f;
             if (ok) {
-                r = p.res[b * p.res_ld + row] + v[b];
+                r = (have ? pre->res[b] : p.res[b * p.res_ld + row]) + v[b];
                 p.y[b * p.y_ld + row] = r;
             }
-            qx_write_group(p.qy, b, g, lane, r, ok);
+            qx_write_group(p.qy, b, g, lane, r, ok, have, have ? pre->nw : 0.0f);
         }
         return;
     }
@@ -514,7 +524,7 @@ __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t
     for (int b = 0; b < B; ++b) {
         if (b >= p.batch) break;
         float r = v[b];
-        if (epi == EPI_ADD) r = p.res[b * p.res_ld + row] + r;
+        if (epi == EPI_ADD) r = (have ? pre->res[b] : p.res[b * p.res_ld + row]) + r;
         p.y[b * p.y_ld + row] = r;
     }
 }

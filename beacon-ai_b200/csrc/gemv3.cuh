@@ -342,14 +342,15 @@ struct G3Range {
 template <int B>
 __device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t KT,
                                                 const G3Range& r, int lane, float (&acc)[B],
-                                                const float (&inv)[B], float* red, int* cnt) {
+                                                const float (&inv)[B], float* red, int* cnt,
+                                                const EpiPre<B>& pre) {
     const GemvParams& p = a.p;
     const uint32_t g0 = g * KT, g1 = g0 + KT;
     float v[B];
     if (g0 >= r.wb && g1 <= r.we) {
 #pragma unroll
         for (int b = 0; b < B; ++b) v[b] = acc[b] * inv[b];
-        gemv_store<B>(p, epi, g, lane, v);
+        gemv_store<B>(p, epi, g, lane, v, &pre);
         return;
     }
     // level 1: the CTA's warps holding part of g, [wf, wl]
@@ -380,7 +381,7 @@ __device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, u
     if (g0 >= r.cb && g1 <= r.ce) {
 #pragma unroll
         for (int b = 0; b < B; ++b) v[b] *= inv[b];
-        gemv_store<B>(p, epi, g, lane, v);
+        gemv_store<B>(p, epi, g, lane, v, &pre);
         return;
     }
     // level 2: the CTAs holding part of g, [cf, cl]
@@ -421,7 +422,7 @@ __device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, u
     }
 #pragma unroll
     for (int b = 0; b < B; ++b) v[b] *= inv[b];
-    gemv_store<B>(p, epi, g, lane, v);
+    gemv_store<B>(p, epi, g, lane, v, &pre);
     if (lane == 0) a.counters[g] = 0;
 }
 
@@ -480,8 +481,23 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     } else {
         prefetch_norm(p, a.kspan, nwr);
     }
+    // the epilogue operands of the group this warp finishes last: the next
+    // GEMV's norm weight now (a weight), the residual once the wait is over
+    EpiPre<B> pre;
+    const uint32_t g_last = (rg.we - 1) / (uint32_t)a.ktiles;
+    const int64_t pre_row = (int64_t)g_last * 32 + lane;
+    pre.nw = 0.0f;
+#pragma unroll
+    for (int b = 0; b < B; ++b) pre.res[b] = 0.0f;
+    if (epi == EPI_ADD && p.qy.data && p.qy.norm_w && pre_row < p.n) pre.nw = __ldg(&p.qy.norm_w[pre_row]);
     pdl_trigger();
     pdl_wait();
+    if (epi == EPI_ADD && p.res) {
+        pre.g = g_last;
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+            pre.res[b] = (b < p.batch && pre_row < p.n) ? __ldcg(&p.res[b * p.res_ld + pre_row]) : 0.0f;
+    }
     if (from_image) {
         // the producer's staging image: bulk copies, and 1/rms from its block sums
         __syncthreads();
@@ -533,7 +549,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
         g3_consume_tile<FMT, MODE, B>(tile, xs, a.kspan, (int)t, acc, rtz);
         // end of a row group (or of this warp's range): finish it
         if (t == KT - 1 || i == n - 1) {
-            g3_finish_group<B>(a, epi, g, KT, rg, lane, acc, inv, red, cta_cnt);
+            g3_finish_group<B>(a, epi, g, KT, rg, lane, acc, inv, red, cta_cnt, pre);
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = 0.0f;
         }

@@ -15,10 +15,12 @@ namespace bc {
 // x * norm_w with the scale absmax / 32767 (the consumer's own rule), their
 // sum, and the sum of squares of x for the consumer's RMSNorm. All 32 lanes
 // take part; `valid` = the row exists (zero otherwise).
-__device__ __forceinline__ void qx_write_group(const QxImage& q, int b, int64_t g, int lane, float x, bool valid) {
+// has_nw: the caller loaded this lane's norm weight ahead (nw), else it is read here.
+__device__ __forceinline__ void qx_write_group(const QxImage& q, int b, int64_t g, int lane, float x, bool valid,
+                                               bool has_nw = false, float nw = 0.0f) {
     const int64_t row = g * 32 + lane;
     const float xv = valid ? x : 0.0f;
-    const float yv = (valid && q.norm_w) ? xv * q.norm_w[row] : xv;
+    const float yv = (valid && q.norm_w) ? xv * (has_nw ? nw : q.norm_w[row]) : xv;
     float am = fabsf(yv);
 #pragma unroll
     for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
