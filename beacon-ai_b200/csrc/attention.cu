@@ -468,7 +468,26 @@ __global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const 
 }
 
 template <int D, int G>
+__global__ void __launch_bounds__(kAttThreads, 1) decode_attn_tc_kernel(const DecodeAttnArgs a) {
+    extern __shared__ __align__(128) uint8_t att_smem[];
+    __shared__ __align__(8) uint64_t bars[kTcStages];
+    attn_unit_tc<D, G>(a, blockIdx.x, blockIdx.y, att_smem, bars, [] {
+        pdl_trigger();
+        pdl_wait();
+    });
+}
+
+template <int D, int G>
+void launch_decode_tc_t(const DecodeAttnArgs& a, cudaStream_t s, bool pdl) {
+    auto kern = decode_attn_tc_kernel<D, G>;
+    BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcLayout<D>::smem));
+    dim3 grid((unsigned)(a.batch * a.kv_heads), (unsigned)a.nsplit);
+    launch_kernel(kern, grid, dim3(kAttThreads), TcLayout<D>::smem, s, pdl, a);
+}
+
+template <int D, int G>
 void launch_decode_bulk_t(const DecodeAttnArgs& a, cudaStream_t s, bool pdl) {
+    if (a.tc) return launch_decode_tc_t<D, G>(a, s, pdl);
     auto kern = decode_attn_bulk_kernel<D, G>;
     BC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AttLayout<D>::smem));
     dim3 grid((unsigned)(a.batch * a.kv_heads), (unsigned)a.nsplit);

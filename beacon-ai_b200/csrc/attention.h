@@ -56,6 +56,7 @@ struct DecodeAttnArgs {
     int* counters;  // [batch * kv_heads] arrival counters, zero at rest (f16 caches)
     int* err;       // set to 3 when a bounded wait gives up (f16 caches)
     QxImage qy;     // f16 caches: also write the output quantised for the o projection
+    int tc = 0;     // f16 caches, fast numerics: the tensor-core kernel
 };
 constexpr int kMaxDecodeSplits = 64;
 constexpr int kMaxBulkSplits = 256;

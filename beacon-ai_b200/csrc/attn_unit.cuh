@@ -50,6 +50,108 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// The split partials of one (sequence, KV head) were stored by its units;
+// this unit's arrival is counted and the last unit to arrive merges them in
+// split order into out (and the o projection's quantised image). Whole CTA of
+// kAttThreads threads; m_s, l_s: G floats of shared memory; flag_s one int.
+template <int D, int G>
+__device__ __forceinline__ void attn_split_merge(const DecodeAttnArgs& a, int b, int kvh, int bk, uint8_t* att_smem,
+                                                 float* m_s, float* l_s, int& flag_s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __syncthreads();  // every partial store precedes thread 0's release
+    if (tid == 0) flag_s = atomic_add_acq_rel_gpu(&a.counters[bk], 1) == a.nsplit - 1;
+    __syncthreads();
+    if (!flag_s) return;
+    // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+    // in split order, MR splits per round (32 while a thread's share of the
+    // round fits in 64 registers, else 16). The first round's partial sums and
+    // every split's m and l are requested together, so the common case (up to
+    // MR splits) costs one round trip to L2.
+    static_assert(G <= kAttWarps, "one head per warp in the merge");
+    const int ns = a.nsplit;
+    constexpr int OPT = (G * D + kAttThreads - 1) / kAttThreads;        // outputs per thread
+    constexpr int MR = OPT <= 2 ? 32 : 16;                              // splits per round
+    float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][MR]
+    float o[OPT], pa[OPT][MR];
+#pragma unroll
+    for (int t = 0; t < OPT; ++t) o[t] = 0.0f;
+    auto load_round = [&](int s0) {
+        const int nr = min(MR, ns - s0);
+#pragma unroll
+        for (int t = 0; t < OPT; ++t) {
+            const int i = tid + t * kAttThreads;
+            const int g = i / D, dd = i - g * D;
+            const int64_t hb = (int64_t)b * a.heads + kvh * G + (g < G ? g : 0);
+#pragma unroll
+            for (int u = 0; u < MR; ++u)
+                pa[t][u] = (i < G * D && u < nr) ? __ldcg(&a.part_acc[(hb * ns + s0 + u) * D + dd]) : 0.0f;
+        }
+    };
+    load_round(0);
+    // warp g < G: head g. Lane j holds split j's m and l when there are at
+    // most 32 splits (else they are re-read per round).
+    const int64_t hbw = (int64_t)b * a.heads + kvh * G + (warp < G ? warp : 0);
+    float mreg = -INFINITY, lreg = 0.0f;
+    if (warp < G) {
+        if (lane < ns) {
+            mreg = __ldcg(&a.part_m[hbw * ns + lane]);
+            lreg = __ldcg(&a.part_l[hbw * ns + lane]);
+        }
+        float M = mreg;
+        for (int s2 = lane + 32; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hbw * ns + s2]));
+        M = warp_max(M);
+        if (lane == 0) {
+            m_s[warp] = M;
+            l_s[warp] = 0.0f;
+        }
+    }
+    __syncthreads();
+    for (int s0 = 0; s0 < ns; s0 += MR) {
+        const int nr = min(MR, ns - s0);
+        if (s0 > 0) load_round(s0);
+        if (warp < G) {
+            float mm, ll;
+            if (ns <= 32) {
+                mm = __shfl_sync(0xffffffffu, mreg, (s0 + lane) & 31);
+                ll = __shfl_sync(0xffffffffu, lreg, (s0 + lane) & 31);
+            } else {
+                mm = lane < nr ? __ldcg(&a.part_m[hbw * ns + s0 + lane]) : -INFINITY;
+                ll = lane < nr ? __ldcg(&a.part_l[hbw * ns + s0 + lane]) : 0.0f;
+            }
+            float w = 0.0f, lw = 0.0f;
+            if (lane < nr) {
+                w = mm == -INFINITY ? 0.0f : expf(mm - m_s[warp]);
+                lw = ll * w;
+            }
+            if (lane < MR) wts[warp * MR + lane] = w;
+            lw = warp_sum(lw);
+            if (lane == 0) l_s[warp] += lw;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < OPT; ++t) {
+            const int i = tid + t * kAttThreads;
+            const int g = i / D;
+            if (i < G * D)
+#pragma unroll
+                for (int u = 0; u < MR; ++u)
+                    if (u < nr) o[t] = fmaf(pa[t][u], wts[g * MR + u], o[t]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int t = 0; t < OPT; ++t) {
+        const int i = tid + t * kAttThreads;
+        if (i >= G * D) continue;
+        const int g = i / D, dd = i - g * D;
+        const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
+        const float r = o[t] * (1.0f / l_s[g]);
+        a.out[hb * D + dd] = r;
+        if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
+    }
+    if (tid == 0) a.counters[bk] = 0;
+}
+
 // One (sequence, KV head, split) unit on the whole CTA (kAttThreads threads):
 // ring = ST stages of staged K/V rows, bars = ST mbarriers (initialised here).
 // wait() separates the requests that depend on nothing in flight from the
@@ -256,98 +358,259 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
         }
     }
     if (a.nsplit == 1) return;
-    __syncthreads();  // every partial store precedes thread 0's release
-    if (tid == 0) flag_s = atomic_add_acq_rel_gpu(&a.counters[bk], 1) == a.nsplit - 1;
-    __syncthreads();
-    if (!flag_s) return;
-    // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-    // in split order, MR splits per round (32 while a thread's share of the
-    // round fits in 64 registers, else 16). The first round's partial sums and
-    // every split's m and l are requested together, so the common case (up to
-    // MR splits) costs one round trip to L2.
-    static_assert(G <= kAttWarps, "one head per warp in the merge");
-    const int ns = a.nsplit;
-    constexpr int OPT = (G * D + kAttThreads - 1) / kAttThreads;        // outputs per thread
-    constexpr int MR = OPT <= 2 ? 32 : 16;                              // splits per round
-    float* wts = reinterpret_cast<float*>(att_smem) + kAttWarps * G * D;  // [G][MR]
-    float o[OPT], pa[OPT][MR];
-#pragma unroll
-    for (int t = 0; t < OPT; ++t) o[t] = 0.0f;
-    auto load_round = [&](int s0) {
-        const int nr = min(MR, ns - s0);
-#pragma unroll
-        for (int t = 0; t < OPT; ++t) {
-            const int i = tid + t * kAttThreads;
-            const int g = i / D, dd = i - g * D;
-            const int64_t hb = (int64_t)b * a.heads + kvh * G + (g < G ? g : 0);
-#pragma unroll
-            for (int u = 0; u < MR; ++u)
-                pa[t][u] = (i < G * D && u < nr) ? __ldcg(&a.part_acc[(hb * ns + s0 + u) * D + dd]) : 0.0f;
+    attn_split_merge<D, G>(a, b, kvh, bk, att_smem, m_s, l_s, flag_s);
+}
+
+// Decode attention on the tensor cores (fast numerics) ------------------------
+// Same unit and split merge as above; the dot products run as warp-level
+// m16n8k16 f16 MMAs with f32 accumulation. Stages hold 128 keys (16 per warp)
+// whose K and V rows are staged with 16-byte chunks at swizzled positions
+// (chunk ^ (row & 7)) so the 8x8 ldmatrix loads are free of bank conflicts.
+// Each warp keeps its own online softmax over its keys: scores S^T = Q K^T
+// with the G query heads as MMA rows (rows G..15 zero) and the query split
+// into f16 high and low parts (two MMAs, ~22-bit query precision), then
+// O += P V with P rounded to f16 straight from the score accumulators. The
+// warps' (m, l, O) are combined at the end in warp order.
+constexpr int kTcKeys = 128;   // keys per stage: 16 per warp
+constexpr int kTcStages = 2;
+
+template <int D>
+struct TcLayout {
+    static constexpr int row = 2 * D;                   // bytes of one key or value row
+    static constexpr int stage = 2 * kTcKeys * row;     // keys, then values
+    static constexpr int chunks = stage / 16;           // 16-byte copies per stage
+    static constexpr size_t smem = (size_t)kTcStages * stage;
+};
+
+__device__ __forceinline__ uint32_t tc_swz(int row, int chunk, int row_bytes) {
+    return (uint32_t)(row * row_bytes + ((chunk ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+// d += A B for one m16n8k16 tile; A rows 8..15 are zero here (a1 = a3 = 0)
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int D, int G, typename Wait>
+__device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, int split, uint8_t* att_smem,
+                                             uint64_t* bars, Wait wait) {
+    static_assert(G <= 8 && (D == 64 || D == 128), "tensor-core decode attention shape");
+    using Lay = TcLayout<D>;
+    constexpr int KS = D / 16;  // MMA k-steps over the head dims
+    constexpr int NT = D / 8;   // 8-dim output tiles
+    constexpr int CPR = D / 8;  // 16-byte chunks per row
+    __shared__ float m_s[G], l_s[G];
+    __shared__ int flag_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int b = bk / a.kv_heads, kvh = bk - b * a.kv_heads;
+    const int kv_len = max(1, min(a.max_kv, a.pos_ptr ? *a.pos_ptr + 1 : a.kv_len));
+    const int chunk = (kv_len + a.nsplit - 1) / a.nsplit;
+    const int k0 = min(kv_len, split * chunk), k1 = min(kv_len, k0 + chunk);
+    const int nkeys = k1 - k0;
+    const int nsteps = (nkeys + kTcKeys - 1) / kTcKeys;
+    const int cur = kv_len - 1;
+    const int cur_step = (cur >= k0 && cur < k1) ? (cur - k0) / kTcKeys : -1;
+    const int64_t ks = (int64_t)a.kv_heads * D;
+    const __half* kc = reinterpret_cast<const __half*>(a.k_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    const __half* vc = reinterpret_cast<const __half*>(a.v_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
+    // chunk c of a stage: row c / CPR of the keys (rows 0..127) then of the values
+    auto issue = [&](int s, bool skip_cur) {
+        uint8_t* base = att_smem + (size_t)(s % kTcStages) * Lay::stage;
+        for (int c = tid; c < Lay::chunks; c += kAttThreads) {
+            const int row = c / CPR, part = c - row * CPR;
+            const int r = row & (kTcKeys - 1);
+            const int key = k0 + s * kTcKeys + r;
+            uint8_t* dst = base + (row < kTcKeys ? 0 : kTcKeys * Lay::row) + tc_swz(r, part, Lay::row);
+            if (key >= k1) {
+                // rows past the split feed the MMAs with probability 0: keep them finite
+                *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+                continue;
+            }
+            if (skip_cur && key == cur) continue;
+            cp_async16(dst, (row < kTcKeys ? kc : vc) + key * ks + part * 8);
         }
     };
-    load_round(0);
-    // warp g < G: head g. Lane j holds split j's m and l when there are at
-    // most 32 splits (else they are re-read per round).
-    const int64_t hbw = (int64_t)b * a.heads + kvh * G + (warp < G ? warp : 0);
-    float mreg = -INFINITY, lreg = 0.0f;
-    if (warp < G) {
-        if (lane < ns) {
-            mreg = __ldcg(&a.part_m[hbw * ns + lane]);
-            lreg = __ldcg(&a.part_l[hbw * ns + lane]);
+    const int npre = min(kTcStages, nsteps);
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; ++s) mbar_init(&bars[s], kAttThreads);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    for (int s = 0; s < npre; ++s) {
+        issue(s, true);
+        if (s != cur_step || tid >= 2 * CPR) cp_async_arrive(&bars[s]);
+    }
+    wait();
+    if (cur_step >= 0 && cur_step < npre && tid < 2 * CPR) {
+        uint8_t* base = att_smem + (size_t)cur_step * Lay::stage;
+        const int r = cur - k0 - cur_step * kTcKeys;
+        const bool is_k = tid < CPR;
+        const int part = is_k ? tid : tid - CPR;
+        cp_async16(base + (is_k ? 0 : kTcKeys * Lay::row) + tc_swz(r, part, Lay::row),
+                   (is_k ? kc : vc) + cur * ks + part * 8);
+        cp_async_arrive(&bars[cur_step]);
+    }
+    // query fragments (MMA rows = heads): this lane's head h = lane / 4, dims
+    // 16 j + 2 (lane % 4) + {0, 1} and + 8, pre-scaled, as f16 high + low parts
+    const int h = lane >> 2, q4 = lane & 3;
+    uint32_t qh0[KS], qh2[KS], ql0[KS], ql2[KS];
+    {
+        const float* qrow = a.q + ((int64_t)b * a.heads + kvh * G + (h < G ? h : 0)) * D;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            float x[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int d = 16 * j + 2 * q4 + (e & 1) + (e >> 1) * 8;
+                x[e] = h < G ? qrow[d] * a.scale : 0.0f;
+            }
+            const __half2 h01 = __floats2half2_rn(x[0], x[1]), h23 = __floats2half2_rn(x[2], x[3]);
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            qh0[j] = *reinterpret_cast<const uint32_t*>(&h01);
+            qh2[j] = *reinterpret_cast<const uint32_t*>(&h23);
+            ql0[j] = pack_f16x2(x[0] - f01.x, x[1] - f01.y);
+            ql2[j] = pack_f16x2(x[2] - f23.x, x[3] - f23.y);
         }
-        float M = mreg;
-        for (int s2 = lane + 32; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hbw * ns + s2]));
-        M = warp_max(M);
-        if (lane == 0) {
-            m_s[warp] = M;
-            l_s[warp] = 0.0f;
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;
+    const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: the matrix this lane addresses, its row
+    int s = 0;
+    bool failed = false;
+    for (; s < nsteps; ++s) {
+        const int st = s % kTcStages;
+        if (!mbar_wait_bounded(&bars[st], (uint32_t)((s / kTcStages) & 1))) failed = true;
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+        const int kt = warp * 16;                               // this warp's 16 keys of the stage
+        const int nv = min(kTcKeys, nkeys - s * kTcKeys) - kt;  // of which valid
+        if (nv > 0) {
+            const uint32_t kbase = smem_u32(att_smem + (size_t)st * Lay::stage);
+            const uint32_t vbase = kbase + kTcKeys * Lay::row;
+            // scores: n-tile 0 = keys kt..kt+7, n-tile 1 = keys kt+8..kt+15
+            float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const int krow = kt + (mi >> 1) * 8 + rr;
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4(kbase + tc_swz(krow, 2 * j + (mi & 1), Lay::row), b00, b01, b10, b11);
+                mma_f16(s0, qh0[j], qh2[j], b00, b01);
+                mma_f16(s1, qh0[j], qh2[j], b10, b11);
+                mma_f16(s0, ql0[j], ql2[j], b00, b01);
+                mma_f16(s1, ql0[j], ql2[j], b10, b11);
+            }
+            // online softmax of head h over this warp's keys (quad lanes share a head)
+            const int c0 = 2 * q4;
+            float v[4] = {s0[0], s0[1], s1[0], s1[1]};
+            const int kk[4] = {c0, c0 + 1, 8 + c0, 9 + c0};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (kk[e] >= nv) v[e] = -INFINITY;
+            float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(m_run, mx);  // finite: every tile has a valid key
+            const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - mn);
+            float p[4], rs = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                p[e] = v[e] == -INFINITY ? 0.0f : expf(v[e] - mn);
+                rs += p[e];
+            }
+            rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+            l_run = l_run * corr + rs;
+            m_run = mn;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                o[t][0] *= corr;
+                o[t][1] *= corr;
+            }
+            // O += P V: P (heads x 16 keys) from the score accumulators
+            const uint32_t pa0 = pack_f16x2(p[0], p[1]), pa2 = pack_f16x2(p[2], p[3]);
+            const int vrow = kt + (mi & 1) * 8 + rr;
+#pragma unroll
+            for (int t = 0; t < NT; t += 2) {
+                uint32_t b0a, b1a, b0b, b1b;
+                ldsm_x4_t(vbase + tc_swz(vrow, t + (mi >> 1), Lay::row), b0a, b1a, b0b, b1b);
+                mma_f16(o[t], pa0, pa2, b0a, b1a);
+                mma_f16(o[t + 1], pa0, pa2, b0b, b1b);
+            }
+        }
+        if (s + kTcStages < nsteps) {
+            __syncthreads();  // every warp is done with stage st
+            issue(s + kTcStages, false);
+            cp_async_arrive(&bars[st]);
+        }
+    }
+    if (failed) {
+        for (int s2 = s; s2 < nsteps && s2 < s + kTcStages; ++s2)
+            mbar_wait_bounded(&bars[s2 % kTcStages], (uint32_t)((s2 / kTcStages) & 1));
+        if (tid == 0) atomicExch(a.err, 3);
+        return;
+    }
+    // combine the warps in warp order (the ring is idle now)
+    __syncthreads();
+    float* wo = reinterpret_cast<float*>(att_smem);       // [warps][G][D]
+    float* wm = wo + kAttWarps * G * D;                    // [warps][G]
+    float* wl = wm + kAttWarps * G;                        // [warps][G]
+    if (h < G) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            wo[(warp * G + h) * D + 8 * t + 2 * q4] = o[t][0];
+            wo[(warp * G + h) * D + 8 * t + 2 * q4 + 1] = o[t][1];
+        }
+        if (q4 == 0) {
+            wm[warp * G + h] = m_run;
+            wl[warp * G + h] = l_run;
         }
     }
     __syncthreads();
-    for (int s0 = 0; s0 < ns; s0 += MR) {
-        const int nr = min(MR, ns - s0);
-        if (s0 > 0) load_round(s0);
-        if (warp < G) {
-            float mm, ll;
-            if (ns <= 32) {
-                mm = __shfl_sync(0xffffffffu, mreg, (s0 + lane) & 31);
-                ll = __shfl_sync(0xffffffffu, lreg, (s0 + lane) & 31);
-            } else {
-                mm = lane < nr ? __ldcg(&a.part_m[hbw * ns + s0 + lane]) : -INFINITY;
-                ll = lane < nr ? __ldcg(&a.part_l[hbw * ns + s0 + lane]) : 0.0f;
-            }
-            float w = 0.0f, lw = 0.0f;
-            if (lane < nr) {
-                w = mm == -INFINITY ? 0.0f : expf(mm - m_s[warp]);
-                lw = ll * w;
-            }
-            if (lane < MR) wts[warp * MR + lane] = w;
-            lw = warp_sum(lw);
-            if (lane == 0) l_s[warp] += lw;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int t = 0; t < OPT; ++t) {
-            const int i = tid + t * kAttThreads;
-            const int g = i / D;
-            if (i < G * D)
-#pragma unroll
-                for (int u = 0; u < MR; ++u)
-                    if (u < nr) o[t] = fmaf(pa[t][u], wts[g * MR + u], o[t]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int t = 0; t < OPT; ++t) {
-        const int i = tid + t * kAttThreads;
-        if (i >= G * D) continue;
+    for (int i = tid; i < G * D; i += kAttThreads) {
         const int g = i / D, dd = i - g * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttWarps; ++w) M = fmaxf(M, wm[w * G + g]);
+        float acc = 0.0f, L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttWarps; ++w) {
+            const float mw = wm[w * G + g];
+            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+            acc = fmaf(wo[(w * G + g) * D + dd], f, acc);
+            L = fmaf(wl[w * G + g], f, L);
+        }
         const int64_t hb = (int64_t)b * a.heads + kvh * G + g;
-        const float r = o[t] * (1.0f / l_s[g]);
-        a.out[hb * D + dd] = r;
-        if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
+        if (a.nsplit == 1) {
+            const float r = acc * (1.0f / L);
+            a.out[hb * D + dd] = r;
+            if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
+        } else {
+            a.part_acc[(hb * a.nsplit + split) * D + dd] = acc;
+            if (dd == 0) {
+                a.part_m[hb * a.nsplit + split] = M;
+                a.part_l[hb * a.nsplit + split] = L;
+            }
+        }
     }
-    if (tid == 0) a.counters[bk] = 0;
+    if (a.nsplit == 1) return;
+    attn_split_merge<D, G>(a, b, kvh, bk, att_smem, m_s, l_s, flag_s);
 }
 
 }  // namespace bc

@@ -359,6 +359,7 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.part_l = m->pl;
             a.out = m->attn;
             if (qxa) a.qy = qx_image(m, 1, m->Lo, rows, nullptr);
+            a.tc = gemv_mode(m) == MODE_FAST ? 1 : 0;
             launch_decode_attention(a, s, m->pdl);
         } else {
             AttnRowsArgs a{};

@@ -181,6 +181,29 @@ def test_literal_cpu_semantics_reproduced(be):
         be.set_numerics(0)
 
 
+@pytest.mark.parametrize("head_dim,kv_heads", [(128, 1), (64, 2)])
+def test_fast_decode_long_context_tensor_core_attention(be, head_dim, kv_heads):
+    """Fast numerics decode over a few hundred cached keys: the tensor-core
+    decode attention (f16 MMAs, split over many CTAs and merged by the last
+    one) keeps the logits within the bar of the oracle's f32 softmax."""
+    from beacon_cuda import _lib as L
+    c = small_cfg(num_layers=2, num_heads=512 // head_dim, num_kv_heads=kv_heads, head_dim=head_dim,
+                  max_context=640)
+    w = make_weights(oracle_cfg(c), orc.Q4_K, seed=77 + head_dim)
+    om = build_oracle_model(oracle_cfg(c), w)
+    m = cuda_model(be, c, w, numerics=L.NUMERICS_FAST, kv_dtype=L.DTYPE_F16)
+    prompt = list(np.random.default_rng(5).integers(0, c["vocab_size"], 450))
+    ref = om.forward(prompt, 0)
+    got = m.forward(prompt, 0)
+    assert np.abs(got[-1] - ref[-1]).max() <= LOGITS_TOL
+    tok, pos = orc.argmax(ref[-1]), len(prompt)
+    for step in range(4):
+        _, lg = m.decode_step([tok], pos, want_logits=True)
+        lo = om.forward([tok], pos)[0]
+        assert np.abs(lg[0] - lo).max() <= LOGITS_TOL, (step, np.abs(lg[0] - lo).max())
+        tok, pos = orc.argmax(lo), pos + 1
+
+
 def test_batched_decode_equals_single_sequences(be):
     from beacon_cuda import _lib as L
     c = small_cfg(num_layers=2, max_context=32)
