@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) decode_attn_bulk_kernel(const 
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttThreads, 1) decode_attn_tc_kernel(const DecodeAttnArgs a) {
+__global__ void __launch_bounds__(kAttThreads, 2) decode_attn_tc_kernel(const DecodeAttnArgs a) {
     extern __shared__ __align__(128) uint8_t att_smem[];
     __shared__ __align__(8) uint64_t bars[kTcStages];
     attn_unit_tc<D, G>(a, blockIdx.x, blockIdx.y, att_smem, bars, [] {

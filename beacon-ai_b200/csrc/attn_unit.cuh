@@ -366,11 +366,11 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
 // m16n8k16 f16 MMAs with f32 accumulation. Stages hold 128 keys (16 per warp)
 // whose K and V rows are staged with 16-byte chunks at swizzled positions
 // (chunk ^ (row & 7)) so the 8x8 ldmatrix loads are free of bank conflicts.
-// Each warp keeps its own online softmax over its keys: scores S^T = Q K^T
-// with the G query heads as MMA rows (rows G..15 zero) and the query split
-// into f16 high and low parts (two MMAs, ~22-bit query precision), then
-// O += P V with P rounded to f16 straight from the score accumulators. The
-// warps' (m, l, O) are combined at the end in warp order.
+// Each warp keeps its own online softmax over its keys, with the G <= 8
+// query heads as the MMA N dimension: scores S = K Q^T (16 keys x 8 heads,
+// the query split into f16 high and low parts, ~22-bit precision), then
+// O^T += V^T P^T with P rounded to f16 and transposed in registers
+// (movmatrix). The warps' (m, l, O) are combined at the end in warp order.
 constexpr int kTcKeys = 128;   // keys per stage: 16 per warp
 constexpr int kTcStages = 2;
 
@@ -393,11 +393,17 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
 }
-// d += A B for one m16n8k16 tile; A rows 8..15 are zero here (a1 = a3 = 0)
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+// d += A B for one m16n8k16 tile
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
@@ -409,8 +415,7 @@ __device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, in
                                              uint64_t* bars, Wait wait) {
     static_assert(G <= 8 && (D == 64 || D == 128), "tensor-core decode attention shape");
     using Lay = TcLayout<D>;
-    constexpr int KS = D / 16;  // MMA k-steps over the head dims
-    constexpr int NT = D / 8;   // 8-dim output tiles
+    constexpr int KS = D / 16;  // 16-dim steps (score k-steps, output m-tiles)
     constexpr int CPR = D / 8;  // 16-byte chunks per row
     __shared__ float m_s[G], l_s[G];
     __shared__ int flag_s;
@@ -426,7 +431,7 @@ __device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, in
     const int64_t ks = (int64_t)a.kv_heads * D;
     const __half* kc = reinterpret_cast<const __half*>(a.k_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
     const __half* vc = reinterpret_cast<const __half*>(a.v_cache) + (int64_t)b * a.cache_sb + (int64_t)kvh * D;
-    // chunk c of a stage: row c / CPR of the keys (rows 0..127) then of the values
+    // chunk c of a stage: row c / CPR of the keys (rows 0..127), then of the values
     auto issue = [&](int s, bool skip_cur) {
         uint8_t* base = att_smem + (size_t)(s % kTcStages) * Lay::stage;
         for (int c = tid; c < Lay::chunks; c += kAttThreads) {
@@ -463,32 +468,33 @@ __device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, in
                    (is_k ? kc : vc) + cur * ks + part * 8);
         cp_async_arrive(&bars[cur_step]);
     }
-    // query fragments (MMA rows = heads): this lane's head h = lane / 4, dims
+    // query fragments (MMA B operand, N = heads): head hq = lane / 4, dims
     // 16 j + 2 (lane % 4) + {0, 1} and + 8, pre-scaled, as f16 high + low parts
-    const int h = lane >> 2, q4 = lane & 3;
-    uint32_t qh0[KS], qh2[KS], ql0[KS], ql2[KS];
+    const int hq = lane >> 2, q4 = lane & 3, r8 = lane >> 2;
+    uint32_t qh0[KS], qh1[KS], ql0[KS], ql1[KS];
     {
-        const float* qrow = a.q + ((int64_t)b * a.heads + kvh * G + (h < G ? h : 0)) * D;
+        const float* qrow = a.q + ((int64_t)b * a.heads + kvh * G + (hq < G ? hq : 0)) * D;
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
             float x[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int d = 16 * j + 2 * q4 + (e & 1) + (e >> 1) * 8;
-                x[e] = h < G ? qrow[d] * a.scale : 0.0f;
+                x[e] = hq < G ? qrow[d] * a.scale : 0.0f;
             }
             const __half2 h01 = __floats2half2_rn(x[0], x[1]), h23 = __floats2half2_rn(x[2], x[3]);
             const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
             qh0[j] = *reinterpret_cast<const uint32_t*>(&h01);
-            qh2[j] = *reinterpret_cast<const uint32_t*>(&h23);
+            qh1[j] = *reinterpret_cast<const uint32_t*>(&h23);
             ql0[j] = pack_f16x2(x[0] - f01.x, x[1] - f01.y);
-            ql2[j] = pack_f16x2(x[2] - f23.x, x[3] - f23.y);
+            ql1[j] = pack_f16x2(x[2] - f23.x, x[3] - f23.y);
         }
     }
-    float o[NT][4];
+    // O^T accumulators: m-tile t = dims 16 t + r8 (+8) x heads 2 q4 + {0, 1}
+    float o[KS][4];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;
+    for (int t = 0; t < KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};  // heads 2 q4 + {0, 1}
     const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: the matrix this lane addresses, its row
     int s = 0;
     bool failed = false;
@@ -504,54 +510,52 @@ __device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, in
         if (nv > 0) {
             const uint32_t kbase = smem_u32(att_smem + (size_t)st * Lay::stage);
             const uint32_t vbase = kbase + kTcKeys * Lay::row;
-            // scores: n-tile 0 = keys kt..kt+7, n-tile 1 = keys kt+8..kt+15
-            float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const int krow = kt + (mi >> 1) * 8 + rr;
+            // scores (16 keys x 8 heads): A = K rows via ldmatrix (keys kt.., dims 16 j..)
+            float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const int krow = kt + (mi & 1) * 8 + rr;
 #pragma unroll
             for (int j = 0; j < KS; ++j) {
-                uint32_t b00, b01, b10, b11;
-                ldsm_x4(kbase + tc_swz(krow, 2 * j + (mi & 1), Lay::row), b00, b01, b10, b11);
-                mma_f16(s0, qh0[j], qh2[j], b00, b01);
-                mma_f16(s1, qh0[j], qh2[j], b10, b11);
-                mma_f16(s0, ql0[j], ql2[j], b00, b01);
-                mma_f16(s1, ql0[j], ql2[j], b10, b11);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(kbase + tc_swz(krow, 2 * j + (mi >> 1), Lay::row), a0, a1, a2, a3);
+                mma_f16(sc, a0, a1, a2, a3, qh0[j], qh1[j]);
+                mma_f16(sc, a0, a1, a2, a3, ql0[j], ql1[j]);
             }
-            // online softmax of head h over this warp's keys (quad lanes share a head)
-            const int c0 = 2 * q4;
-            float v[4] = {s0[0], s0[1], s1[0], s1[1]};
-            const int kk[4] = {c0, c0 + 1, 8 + c0, 9 + c0};
+            // sc: keys r8 (sc[0..1]) and r8 + 8 (sc[2..3]) x heads 2 q4 + {0, 1};
+            // online softmax per head over the 8 lanes that share q4
+            if (r8 >= nv) sc[0] = sc[1] = -INFINITY;
+            if (r8 + 8 >= nv) sc[2] = sc[3] = -INFINITY;
+            float p[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                if (kk[e] >= nv) v[e] = -INFINITY;
-            float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float mn = fmaxf(m_run, mx);  // finite: every tile has a valid key
-            const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - mn);
-            float p[4], rs = 0.0f;
+            for (int c = 0; c < 2; ++c) {
+                float mx = fmaxf(sc[c], sc[2 + c]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(m_run[c], mx);  // finite: every tile has a valid key
+                const float corr = m_run[c] == -INFINITY ? 0.0f : expf(m_run[c] - mn);
+                p[c] = sc[c] == -INFINITY ? 0.0f : expf(sc[c] - mn);
+                p[2 + c] = sc[2 + c] == -INFINITY ? 0.0f : expf(sc[2 + c] - mn);
+                float rs = p[c] + p[2 + c];
+                rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 16);
+                l_run[c] = l_run[c] * corr + rs;
+                m_run[c] = mn;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                p[e] = v[e] == -INFINITY ? 0.0f : expf(v[e] - mn);
-                rs += p[e];
+                for (int t = 0; t < KS; ++t) {
+                    o[t][c] *= corr;
+                    o[t][2 + c] *= corr;
+                }
             }
-            rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-            l_run = l_run * corr + rs;
-            m_run = mn;
+            // P^T (16 keys x 8 heads) as the B operand: transpose the two 8x8 blocks
+            const uint32_t pb0 = movm_t(pack_f16x2(p[0], p[1])), pb1 = movm_t(pack_f16x2(p[2], p[3]));
+            // O^T += V^T P^T: A = V^T via transposing ldmatrix (dims 16 t.., keys kt..)
+            const int vrow = kt + (mi >> 1) * 8 + rr;
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                o[t][0] *= corr;
-                o[t][1] *= corr;
-            }
-            // O += P V: P (heads x 16 keys) from the score accumulators
-            const uint32_t pa0 = pack_f16x2(p[0], p[1]), pa2 = pack_f16x2(p[2], p[3]);
-            const int vrow = kt + (mi & 1) * 8 + rr;
-#pragma unroll
-            for (int t = 0; t < NT; t += 2) {
-                uint32_t b0a, b1a, b0b, b1b;
-                ldsm_x4_t(vbase + tc_swz(vrow, t + (mi >> 1), Lay::row), b0a, b1a, b0b, b1b);
-                mma_f16(o[t], pa0, pa2, b0a, b1a);
-                mma_f16(o[t + 1], pa0, pa2, b0b, b1b);
+            for (int t = 0; t < KS; ++t) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(vbase + tc_swz(vrow, 2 * t + (mi & 1), Lay::row), a0, a1, a2, a3);
+                mma_f16(o[t], a0, a1, a2, a3, pb0, pb1);
             }
         }
         if (s + kTcStages < nsteps) {
@@ -571,15 +575,19 @@ __device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, in
     float* wo = reinterpret_cast<float*>(att_smem);       // [warps][G][D]
     float* wm = wo + kAttWarps * G * D;                    // [warps][G]
     float* wl = wm + kAttWarps * G;                        // [warps][G]
-    if (h < G) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            wo[(warp * G + h) * D + 8 * t + 2 * q4] = o[t][0];
-            wo[(warp * G + h) * D + 8 * t + 2 * q4 + 1] = o[t][1];
-        }
-        if (q4 == 0) {
-            wm[warp * G + h] = m_run;
-            wl[warp * G + h] = l_run;
+    for (int c = 0; c < 2; ++c) {
+        const int hh = 2 * q4 + c;
+        if (hh < G) {
+#pragma unroll
+            for (int t = 0; t < KS; ++t) {
+                wo[(warp * G + hh) * D + 16 * t + r8] = o[t][c];
+                wo[(warp * G + hh) * D + 16 * t + r8 + 8] = o[t][2 + c];
+            }
+            if (r8 == 0) {
+                wm[warp * G + hh] = m_run[c];
+                wl[warp * G + hh] = l_run[c];
+            }
         }
     }
     __syncthreads();
