@@ -50,6 +50,77 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Split partials that fit the ring (both decode kernels' rings hold at
+// least 1024 * D bytes) are merged from shared memory, fetched with one bulk
+// copy per head: the copy engine keeps them all in flight, where a thread's
+// share of hundreds of loads would queue behind its SM's outstanding-request
+// limit.
+template <int D>
+constexpr size_t merge_bulk_cap() { return (size_t)1024 * D - 1024; }
+
+// The merge of attn_split_merge from shared memory: the last CTA of (b, kvh)
+// copies the G heads' [nsplit][D] partial sums into att_smem, reads every
+// split's m and l, and sums in split order. Whole CTA; G * nsplit * (D + 1)
+// floats fit in merge_bulk_cap<D>().
+template <int D, int G>
+__device__ __forceinline__ void attn_split_merge_bulk(const DecodeAttnArgs& a, int b, int kvh, int bk,
+                                                      uint8_t* att_smem, float* m_s, float* l_s) {
+    __shared__ __align__(8) uint64_t mbar;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ns = a.nsplit;
+    float* pbuf = reinterpret_cast<float*>(att_smem);  // [G][ns][D]
+    float* wts = pbuf + (size_t)G * ns * D;            // [G][ns]
+    const int64_t hb0 = (int64_t)b * a.heads + kvh * G;
+    if (tid == 0) {
+        mbar_init(&mbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // the ring was last used, and the other units' partials were written
+        // (acquired above), through the generic proxy; the copies use the async one
+        asm volatile("fence.proxy.async;" ::: "memory");
+        const uint32_t per = (uint32_t)ns * D * 4;
+        mbar_expect_tx(&mbar, per * G);
+        for (int g = 0; g < G; ++g)
+            bulk_g2s(pbuf + (size_t)g * ns * D, a.part_acc + (hb0 + g) * ns * D, per, &mbar);
+    }
+    // warp g < G: head g's weights e^(m_s - M) and l = sum_s l_s e^(m_s - M)
+    if (warp < G) {
+        const int64_t hb = hb0 + warp;
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(&a.part_m[hb * ns + s2]));
+        M = warp_max(M);
+        float lw = 0.0f;
+        for (int s2 = lane; s2 < ns; s2 += 32) {
+            const float mm = __ldcg(&a.part_m[hb * ns + s2]);
+            const float w = mm == -INFINITY ? 0.0f : expf(mm - M);
+            wts[warp * ns + s2] = w;
+            lw += __ldcg(&a.part_l[hb * ns + s2]) * w;
+        }
+        lw = warp_sum(lw);
+        if (lane == 0) l_s[warp] = lw;
+    }
+    __syncthreads();  // thread 0's barrier initialisation, the weights
+    const bool ok = mbar_wait_bounded(&mbar, 0);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+            atomicExch(a.err, 3);
+            a.counters[bk] = 0;
+        }
+        return;
+    }
+    for (int i = tid; i < G * D; i += kAttThreads) {
+        const int g = i / D, dd = i - g * D;
+        const float* src = pbuf + (size_t)g * ns * D + dd;
+        const float* w = wts + g * ns;
+        float o = 0.0f;
+        for (int s2 = 0; s2 < ns; ++s2) o = fmaf(src[(size_t)s2 * D], w[s2], o);
+        const float r = o * (1.0f / l_s[g]);
+        a.out[(hb0 + g) * D + dd] = r;
+        // a warp holds 32 consecutive dims of one head: one block of the o input
+        if (a.qy.data) qx_write_group(a.qy, b, ((int64_t)(kvh * G + g) * D + dd) >> 5, lane, r, true);
+    }
+    if (tid == 0) a.counters[bk] = 0;
+}
+
 // The split partials of one (sequence, KV head) were stored by its units;
 // this unit's arrival is counted and the last unit to arrive merges them in
 // split order into out (and the o projection's quantised image). Whole CTA of
@@ -62,6 +133,10 @@ __device__ __forceinline__ void attn_split_merge(const DecodeAttnArgs& a, int b,
     if (tid == 0) flag_s = atomic_add_acq_rel_gpu(&a.counters[bk], 1) == a.nsplit - 1;
     __syncthreads();
     if (!flag_s) return;
+    if ((size_t)G * a.nsplit * (D + 1) * 4 <= merge_bulk_cap<D>()) {
+        attn_split_merge_bulk<D, G>(a, b, kvh, bk, att_smem, m_s, l_s);
+        return;
+    }
     // the last CTA of (b, kvh): out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M)
     // in split order, MR splits per round (32 while a thread's share of the
     // round fits in 64 registers, else 16). The first round's partial sums and

@@ -181,11 +181,14 @@ def test_literal_cpu_semantics_reproduced(be):
         be.set_numerics(0)
 
 
-@pytest.mark.parametrize("head_dim,kv_heads", [(128, 1), (64, 2)])
+@pytest.mark.parametrize("head_dim,kv_heads", [(128, 1), (64, 2), (128, 4), (64, 8)])
 def test_fast_decode_long_context_tensor_core_attention(be, head_dim, kv_heads):
     """Fast numerics decode over a few hundred cached keys: the tensor-core
     decode attention (f16 MMAs, split over many CTAs and merged by the last
-    one) keeps the logits within the bar of the oracle's f32 softmax."""
+    one) keeps the logits within the bar of the oracle's f32 softmax. With
+    more KV heads there are fewer splits per head and the merge reads the
+    partials through bulk copies into shared memory; with fewer, through
+    registers in rounds."""
     from beacon_cuda import _lib as L
     c = small_cfg(num_layers=2, num_heads=512 // head_dim, num_kv_heads=kv_heads, head_dim=head_dim,
                   max_context=640)
