@@ -468,6 +468,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             bulk_g2s(myring + (size_t)i * tb, p.w + (t_begin + i) * tb, (uint32_t)tb, &mybar[i]);
         }
     __shared__ __align__(8) uint64_t qx_bar;
+    __shared__ float inv_s[B];
     float inv[B];  // 1/rms per row when the producer quantised x * norm_w
 #pragma unroll
     for (int b = 0; b < B; ++b) inv[b] = 1.0f;
@@ -507,21 +508,23 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             for (uint32_t off = 0; off < bytes; off += 16384u)
                 bulk_g2s(xs + off, p.qx.data + off, min(16384u, bytes - off), &qx_bar);
         }
-        if (p.qx.ss) {
+        // warp b sums row b's block sums of squares (B <= 8 warps)
+        if (p.qx.ss && warp < B) {
             const int nblk = a.kspan / 32;
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                float t = 0.0f;
-                for (int j = lane; j < nblk; j += 32) t += __ldcg(&p.qx.ss[b * nblk + j]);
-                t = warp_sum(t);
-                inv[b] = 1.0f / sqrtf(t / (float)p.k + p.norm_eps);
-            }
+            float t = 0.0f;
+            for (int j = lane; j < nblk; j += 32) t += __ldcg(&p.qx.ss[warp * nblk + j]);
+            t = warp_sum(t);
+            if (lane == 0) inv_s[warp] = 1.0f / sqrtf(t / (float)p.k + p.norm_eps);
         }
         if (!mbar_wait_bounded(&qx_bar, 0) && lane == 0) atomicExch(a.err, 1);
     } else {
         stage_x_full<FMT, MODE, B>(p, xs, a.kspan, nwr);
     }
     __syncthreads();
+    if (from_image && p.qx.ss) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) inv[b] = inv_s[b];
+    }
 
     float acc[B];
 #pragma unroll
