@@ -439,7 +439,7 @@ __device__ __forceinline__ void swiglu_handoff(const GemvParams& p, int64_t g, i
 // the residual rows and the next GEMV's norm weight.
 template <int B>
 struct EpiPre {
-    int64_t g = -1;  // the group they belong to; -1: none
+    int g = -1;      // the group they belong to; -1: none
     float res[B];
     float nw;
 };
@@ -448,7 +448,7 @@ template <int B>
 __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t g, int lane,
                                            const float (&v)[B], const EpiPre<B>* pre = nullptr) {
     const int64_t row = g * 32 + lane;
-    const bool have = pre && pre->g == g;
+    const bool have = pre && (int64_t)pre->g == g;
     if (epi == EPI_QKV) {
         // the whole warp takes part: pairs (2i, 2i+1) are lanes (l, l ^ 1)
         const QkvEpi& e = p.qkv;

@@ -332,6 +332,23 @@ struct G3Range {
     uint32_t T, C, c, cb, ce, n, w, wb, we;
 };
 
+// This warp's ranges (32-bit tile arithmetic: the host keeps total_tiles *
+// CTAs < 2^32). Recomputed where needed rather than held in registers
+// through the tile loop.
+__device__ __forceinline__ G3Range g3_range(uint32_t T) {
+    G3Range r;
+    r.T = T;
+    r.C = gridDim.x;
+    r.c = blockIdx.x;
+    r.cb = r.c * r.T / r.C;
+    r.ce = (r.c + 1) * r.T / r.C;
+    r.n = r.ce - r.cb;
+    r.w = threadIdx.x >> 5;
+    r.wb = r.cb + r.w * r.n / kG3Warps;
+    r.we = r.cb + (r.w + 1) * r.n / kG3Warps;
+    return r;
+}
+
 // End of row group g in this warp's range: store it if the warp holds all of
 // it; else leave the warp's partial in shared memory, and the last warp of
 // the CTA to arrive sums the CTA's share of g in warp order; if other CTAs
@@ -341,10 +358,11 @@ struct G3Range {
 // epilogue. red: [8 warps][2][B][32] floats; cnt: the CTA's arrival counters.
 template <int B>
 __device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t KT,
-                                                const G3Range& r, int lane, float (&acc)[B],
+                                                int lane, float (&acc)[B],
                                                 const float (&inv)[B], float* red, int* cnt,
                                                 const EpiPre<B>& pre) {
     const GemvParams& p = a.p;
+    const G3Range r = g3_range((uint32_t)a.total_tiles);
     const uint32_t g0 = g * KT, g1 = g0 + KT;
     float v[B];
     if (g0 >= r.wb && g1 <= r.we) {
@@ -442,16 +460,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     uint8_t* myring = ring + (size_t)warp * S * tb;
 
     // 32-bit tile arithmetic (the host keeps total_tiles * CTAs < 2^32)
-    G3Range rg;
-    rg.T = (uint32_t)a.total_tiles;
-    rg.C = gridDim.x;
-    rg.c = blockIdx.x;
-    rg.cb = rg.c * rg.T / rg.C;
-    rg.ce = (rg.c + 1) * rg.T / rg.C;
-    rg.n = rg.ce - rg.cb;
-    rg.w = (uint32_t)warp;
-    rg.wb = rg.cb + rg.w * rg.n / kG3Warps;
-    rg.we = rg.cb + (rg.w + 1) * rg.n / kG3Warps;
+    const G3Range rg = g3_range((uint32_t)a.total_tiles);
     const int64_t t_begin = rg.wb;
     const int n = (int)(rg.we - rg.wb);
     __shared__ int cta_cnt[kG3MaxCtaGroups];  // arrivals per row group of this CTA's range
@@ -494,7 +503,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     pdl_trigger();
     pdl_wait();
     if (epi == EPI_ADD && p.res) {
-        pre.g = g_last;
+        pre.g = (int)g_last;
 #pragma unroll
         for (int b = 0; b < B; ++b)
             pre.res[b] = (b < p.batch && pre_row < p.n) ? __ldcg(&p.res[b * p.res_ld + pre_row]) : 0.0f;
@@ -552,7 +561,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
         g3_consume_tile<FMT, MODE, B>(tile, xs, a.kspan, (int)t, acc, rtz);
         // end of a row group (or of this warp's range): finish it
         if (t == KT - 1 || i == n - 1) {
-            g3_finish_group<B>(a, epi, g, KT, rg, lane, acc, inv, red, cta_cnt, pre);
+            g3_finish_group<B>(a, epi, g, KT, lane, acc, inv, red, cta_cnt, pre);
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = 0.0f;
         }
