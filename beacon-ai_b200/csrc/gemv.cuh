@@ -79,7 +79,7 @@ __device__ __forceinline__ float f16_round_trip_rtz(float v) {
 // F32 mode:  float xs[B][span]
 // FAST mode: int16 xq[B][span] (Q4_0: each 8-element group stored as
 //            e0 e2 e4 e6 e1 e3 e5 e7 to match the interleaved nibbles),
-//            float sx[B][span/32], int sq[B][span/32] (sum of the int16s).
+//            float2 [B][span/32] = (scale, sum of the block's int16 codes).
 template <int FMT, int MODE, int B>
 __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* smem, int64_t k_base,
                                         int span) {
@@ -92,8 +92,7 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* smem, int6
     } else {
         int16_t* xq = reinterpret_cast<int16_t*>(smem);
         const int nblk = span / 32;
-        float* sx = reinterpret_cast<float*>(smem + (size_t)B * span * 2);
-        int* sq = reinterpret_cast<int*>(sx + B * nblk);
+        float2* sxq = reinterpret_cast<float2*>(smem + (size_t)B * span * 2);
         for (int i = threadIdx.x; i < B * nblk; i += blockDim.x) {
             int b = i / nblk, j = i - b * nblk;
             float v[32];
@@ -135,8 +134,7 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* smem, int6
             for (int c = 0; c < 4; ++c)
                 dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
                                     packed[4 * c + 3]);
-            sx[b * nblk + j] = amax > 0.0f ? __fdiv_rn(amax, 32767.0f) : 0.0f;
-            sq[b * nblk + j] = sum;
+            sxq[b * nblk + j] = make_float2(amax > 0.0f ? __fdiv_rn(amax, 32767.0f) : 0.0f, (float)sum);
         }
     }
 }
@@ -211,8 +209,7 @@ __device__ __forceinline__ void consume_q4_0(const uint4& meta, const uint4 (&q)
     } else {
         const int16_t* xq = reinterpret_cast<const int16_t*>(smem);
         const int nblk = span / 32;
-        const float* sx = reinterpret_cast<const float*>(smem + (size_t)B * span * 2);
-        const int* sq = reinterpret_cast<const int*>(sx + B * nblk);
+        const float2* sxq = reinterpret_cast<const float2*>(smem + (size_t)B * span * 2);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             const float d = half_at(meta, c);
@@ -238,7 +235,8 @@ __device__ __forceinline__ void consume_q4_0(const uint4& meta, const uint4 (&q)
                 }
                 const int ai = al + (ah >> 4);
                 const int bi = b * nblk + blk;
-                acc[b] = fmaf(d * sx[bi], (float)(ai - 8 * sq[bi]), acc[b]);
+                const float2 xb = sxq[bi];
+                acc[b] = fmaf(d * xb.x, fmaf(-8.0f, xb.y, (float)ai), acc[b]);
             }
         }
     }
@@ -269,7 +267,7 @@ __device__ __forceinline__ void consume_q8_0(const uint4& meta, const uint4 (&q)
     } else {
         const int16_t* xq = reinterpret_cast<const int16_t*>(smem);
         const int nblk = span / 32;
-        const float* sx = reinterpret_cast<const float*>(smem + (size_t)B * span * 2);
+        const float2* sxq = reinterpret_cast<const float2*>(smem + (size_t)B * span * 2);
 #pragma unroll
         for (int bl = 0; bl < 8; ++bl) {
             const float d = half_at(meta, bl);
@@ -292,7 +290,7 @@ __device__ __forceinline__ void consume_q8_0(const uint4& meta, const uint4 (&q)
                     a2[h] = dp2a_hi_s8(Y.w, wq[3], a2[h]);
                 }
                 const int ai = a2[0] + a2[1];
-                acc[b] = fmaf(d * sx[b * nblk + blk], (float)ai, acc[b]);
+                acc[b] = fmaf(d * sxq[b * nblk + blk].x, (float)ai, acc[b]);
             }
         }
     }
@@ -355,8 +353,16 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
     } else {
         const int16_t* xq = reinterpret_cast<const int16_t*>(smem);
         const int nblk = span / 32;
-        const float* sx = reinterpret_cast<const float*>(smem + (size_t)B * span * 2);
-        const int* sq = reinterpret_cast<const int*>(sx + B * nblk);
+        const float2* sxq = reinterpret_cast<const float2*>(smem + (size_t)B * span * 2);
+        // the eight 6-bit scales and mins as bytes of four words; byte k of a
+        // word becomes a float through 2^23 + byte (one byte permute) - 2^23
+        const uint32_t w0 = meta.y, w1 = meta.z, w2 = meta.w;
+        const uint32_t s03 = w0 & 0x3F3F3F3Fu, m03 = w1 & 0x3F3F3F3Fu;
+        const uint32_t s47 = (w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u);
+        const uint32_t m47 = ((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u);
+        auto byte_f32 = [](uint32_t w, int k) {
+            return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u | (uint32_t)k)) - 8388608.0f;
+        };
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {
             // low nibbles as bytes; high nibbles kept in place (16 x value): the
@@ -370,8 +376,10 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
                     lo[h][wd] = w & 0x0F0F0F0Fu;
                     hi[h][wd] = w & 0xF0F0F0F0u;
                 }
-            const float dl = d * (float)sc[2 * pr], dh = d * (float)sc[2 * pr + 1];
-            const float ml = dmin * (float)mn[2 * pr], mh = dmin * (float)mn[2 * pr + 1];
+            const uint32_t sw = pr < 2 ? s03 : s47, mw = pr < 2 ? m03 : m47;
+            const int k0 = (2 * pr) & 3;
+            const float dl = d * byte_f32(sw, k0), dh = d * byte_f32(sw, k0 + 1);
+            const float ml = dmin * byte_f32(mw, k0), mh = dmin * byte_f32(mw, k0 + 1);
             const int jl = tile * 8 + 2 * pr, jh = jl + 1;
 #pragma unroll
             for (int b = 0; b < B; ++b) {
@@ -399,11 +407,10 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
                     al[h] = dp2a_hi_u8(L1.w, lo[h][3], al[h]);
                     ah[h] = dp2a_hi_u8(H1.w, hi[h][3], ah[h]);
                 }
-                const int sl = al[0] + al[1], sh = (ah[0] + ah[1]) >> 4;
-                const int bl = b * nblk + jl, bh = b * nblk + jh;
-                float v = sx[bl] * (dl * (float)sl - ml * (float)sq[bl]) +
-                          sx[bh] * (dh * (float)sh - mh * (float)sq[bh]);
-                acc[b] += v;
+                const float sl = (float)(al[0] + al[1]), sh = (float)((ah[0] + ah[1]) >> 4);
+                const float2 pl = sxq[b * nblk + jl], ph = sxq[b * nblk + jh];
+                acc[b] = fmaf(pl.x, fmaf(dl, sl, -ml * pl.y), acc[b]);
+                acc[b] = fmaf(ph.x, fmaf(dh, sh, -mh * ph.y), acc[b]);
             }
         }
     }

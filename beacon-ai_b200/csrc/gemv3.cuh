@@ -120,8 +120,7 @@ __device__ __forceinline__ void store_passes(const float4 (&v)[NP], int p0, int 
         return;
     }
     int16_t* xq = reinterpret_cast<int16_t*>(xs) + (size_t)b * kspan;
-    float* sx = reinterpret_cast<float*>(xs + (size_t)B * kspan * 2) + b * nblk;
-    int* sq = reinterpret_cast<int*>(reinterpret_cast<float*>(xs + (size_t)B * kspan * 2) + B * nblk) + b * nblk;
+    float2* sxq = reinterpret_cast<float2*>(xs + (size_t)B * kspan * 2) + b * nblk;  // (scale, code sum)
     float am[NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i) am[i] = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
@@ -160,8 +159,7 @@ __device__ __forceinline__ void store_passes(const float4 (&v)[NP], int p0, int 
         if (c < kspan) {
             *reinterpret_cast<uint2*>(xq + c) = make_uint2(lo, hi);
             if ((tid & 7) == 0) {
-                sx[c >> 5] = am[i] * (1.0f / 32767.0f);
-                sq[c >> 5] = sum[i];
+                sxq[c >> 5] = make_float2(am[i] * (1.0f / 32767.0f), (float)sum[i]);
             }
         }
     }

@@ -23,8 +23,8 @@ enum GemvEpilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
 // position outside [0, max_ctx) sets *err = 2 and writes nothing.
 // Activations quantised by the kernel that produces them (decode, fast
 // numerics): the consumer GEMV's shared-memory staging image, in global
-// memory -- int16 codes [bpad][kspan], f32 block scales [bpad][kspan/32],
-// int32 code sums [bpad][kspan/32] -- plus, when the consumer fuses an
+// memory -- int16 codes [bpad][kspan], then per 32-block of each row the
+// pair (f32 scale, code sum as f32) [bpad][kspan/32] -- plus, when the consumer fuses an
 // RMSNorm, the sums of squares of the unnormalised values per 32-block
 // [bpad][kspan/32] (the codes are then of x * norm_w, and the consumer scales
 // its outputs by 1/rms). The producer writes rows b < batch only; rows

@@ -37,10 +37,8 @@ __device__ __forceinline__ void qx_write_group(const QxImage& q, int b, int64_t 
     const int pos = q.perm ? ((lane & ~7) | ((e & 1) ? 4 + (e >> 1) : (e >> 1))) : lane;
     reinterpret_cast<int16_t*>(q.data)[(int64_t)b * q.kspan + g * 32 + pos] = (int16_t)code;
     if (lane == 0) {
-        float* sx = reinterpret_cast<float*>(q.data + (size_t)q.bpad * q.kspan * 2);
-        int* sq = reinterpret_cast<int*>(sx + q.bpad * nblk);
-        sx[b * nblk + g] = am * (1.0f / 32767.0f);
-        sq[b * nblk + g] = sum;
+        float2* sxq = reinterpret_cast<float2*>(q.data + (size_t)q.bpad * q.kspan * 2);  // (scale, code sum)
+        sxq[b * nblk + g] = make_float2(am * (1.0f / 32767.0f), (float)sum);
         if (q.ss) q.ss[b * nblk + g] = ss;
     }
 }
