@@ -76,7 +76,7 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     pl.v2 = plan_qgemv(ctx, L, batch, mode);
     if (batch > 8) return pl;
     pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : 8;
-    const size_t budget = 200 * 1024, half_sm = 110 * 1024;
+    const size_t budget = 220 * 1024, half_sm = 110 * 1024;
     const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad);
     const size_t tb = (size_t)L.tile_bytes;
     if (xb + 256 + 2 * kG3Warps * tb > budget) return pl;

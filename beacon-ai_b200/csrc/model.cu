@@ -212,7 +212,7 @@ namespace {
 int gemv_mode(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32; }
 bool gemv_rtz(const BeaconCudaModel* m) { return m->cfg.numerics == BEACON_CUDA_NUMERICS_REF_RTZ; }
 
-// y = W x over `rows` rows of x, in chunks of 16 rows (the GEMV batch limit).
+// y = W x over `rows` rows of x, in launches of up to 16 rows (see gemv_rows).
 // The quantised-activation hand-off applies to a decode step of the fast
 // numerics on one GPU whose consumers all run the persistent GEMV and whose
 // attention is the f16-cache kernel (the o input's producer).
@@ -237,6 +237,18 @@ QxImage qx_image(BeaconCudaModel* m, int which, const QLayout& consumer, int row
     return q;
 }
 
+// Rows per GEMV launch: up to 16. Up to 8 rows whose persistent plan does
+// not fit (staged activations of a long K) go in 4-, 2- or 1-row launches
+// that take the persistent kernel -- each reads the weights again, still far
+// faster than the tiled kernel -- else the tiled kernel takes them all.
+int gemv_rows(const BeaconCudaModel* m, const QLayout& L, int rem) {
+    const int b = std::min(16, rem);
+    if (b > 8 || plan_linear(m->ctx, L, b, gemv_mode(m)).v3) return b;
+    for (int c : {4, 2, 1})
+        if (c < b && plan_linear(m->ctx, L, c, gemv_mode(m)).v3) return c;
+    return b;
+}
+
 // qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.
 // More than 16 rows in the fast numerics run as one tensor-core GEMM.
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
@@ -252,8 +264,8 @@ void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x,
                         qkv ? &qe : nullptr);
         return;
     }
-    for (int r0 = 0; r0 < rows; r0 += 16) {
-        const int b = std::min(16, rows - r0);
+    for (int r0 = 0, b = 0; r0 < rows; r0 += b) {
+        b = gemv_rows(m, L, rows - r0);
         LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
         QkvEpi qe;
         if (qkv) {
@@ -278,14 +290,17 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
                    const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
     const int64_t hid = m->cfg.hidden_size;
     bool fused = true;
-    for (int r0 = 0; r0 < rows && fused; r0 += 16) fused = plan_linear(m->ctx, L, std::min(16, rows - r0), gemv_mode(m)).v3;
+    for (int r0 = 0, b = 0; r0 < rows && fused; r0 += b) {
+        b = gemv_rows(m, L, rows - r0);
+        fused = plan_linear(m->ctx, L, b, gemv_mode(m)).v3;
+    }
     if (!fused) {
         rmsnorm(m, x, norm_w, m->xn, rows, s);
         linear(m, L, w, m->xn, hid, rows, y, y_ld, epi, nullptr, 0, s, qkv);
         return;
     }
-    for (int r0 = 0; r0 < rows; r0 += 16) {
-        const int b = std::min(16, rows - r0);
+    for (int r0 = 0, b = 0; r0 < rows; r0 += b) {
+        b = gemv_rows(m, L, rows - r0);
         LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
         QkvEpi qe;
         if (qkv) {
