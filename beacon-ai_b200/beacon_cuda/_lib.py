@@ -64,6 +64,7 @@ SIGNATURES = {
     "beacon_cuda_context_create": (_I32, [_I32, _PP]),
     "beacon_cuda_context_destroy": (None, [_P]),
     "beacon_cuda_context_set_numerics": (_I32, [_P, _I32]),
+    "beacon_cuda_context_set_wait_limit": (_I32, [_P, _I64]),
     "beacon_cuda_stream_create": (_I32, [_P, _PP]),
     "beacon_cuda_stream_wrap": (_I32, [_P, _P, _PP]),
     "beacon_cuda_stream_destroy": (None, [_P]),
@@ -95,6 +96,8 @@ SIGNATURES = {
     "beacon_cuda_op_embedding": (_I32, [_P, _P, _P, _P, _PP]),
     "beacon_cuda_create_token_tensor": (_I32, [_P, _P, _SZ, _PP]),
     "beacon_cuda_op_argmax": (_I32, [_P, _P, _P, _PP]),
+    "beacon_cuda_profile_quantized_matmul": (_I32, [_P, _P, _PP, _I32, _P, _I32, ctypes.POINTER(ctypes.c_float),
+                                                    ctypes.POINTER(ctypes.c_uint64)]),
     "beacon_cuda_op_dequantize_to_f16": (_I32, [_P, _P, _P, _PP]),
     "beacon_cuda_op_quantize": (_I32, [_P, _P, _P, _I32, _I32, _PP]),
     "beacon_cuda_quantize_blocks": (_I32, [_P, _P, _P, _I64, _I64, _I32, _I32, _P]),
@@ -106,6 +109,7 @@ SIGNATURES = {
     "beacon_cuda_model_forward": (_I32, [_P, _P, _P, _I32, _I32, _P]),
     "beacon_cuda_model_decode_step": (_I32, [_P, _P, _P, _I32, _I32, _P, _P]),
     "beacon_cuda_model_decode_step_device": (_I32, [_P, _P, _P, _I32, _I32, _P, _P]),
+    "beacon_cuda_model_synchronize": (_I32, [_P, _P]),
     "beacon_cuda_model_profile_linear": (_I32, [_P, _P, _I32, _I32, _I32, ctypes.POINTER(ctypes.c_float),
                                                 ctypes.POINTER(ctypes.c_uint64)]),
     "beacon_cuda_model_fill_kv_random": (_I32, [_P, _I32, ctypes.c_uint64]),

@@ -157,6 +157,10 @@ class CudaBackend:
     def set_numerics(self, numerics: int) -> None:
         _raise(L.lib().beacon_cuda_context_set_numerics(self.ctx, numerics))
 
+    def set_wait_limit(self, cycles: int) -> None:
+        """Limit (SM clock cycles) of the kernels' bounded waits; 0 = default."""
+        _raise(L.lib().beacon_cuda_context_set_wait_limit(self.ctx, cycles))
+
     def close(self) -> None:
         if self.ctx and self.ctx.value:
             L.lib().beacon_cuda_context_destroy(self.ctx)
@@ -174,6 +178,15 @@ class CudaBackend:
         h = ctypes.c_void_p()
         _raise(L.lib().beacon_cuda_tensor_upload(self.ctx, data.ctypes.data, arr, nd, dtype, nibble_order,
                                                  ctypes.byref(h)))
+        return Tensor(h.value)
+
+    def from_device_blocks(self, device_ptr: int, shape, dtype: int,
+                           nibble_order: int = L.NIBBLE_REF_INTERLEAVED) -> Tensor:
+        """A quantized tensor from raw GGUF block bytes already in device memory."""
+        arr, nd = _shape_arr(shape)
+        h = ctypes.c_void_p()
+        _raise(L.lib().beacon_cuda_tensor_from_device_blocks(self.ctx, ctypes.c_void_p(device_ptr), arr, nd, dtype,
+                                                             nibble_order, ctypes.byref(h)))
         return Tensor(h.value)
 
     def zeros(self, shape, dtype: int = L.DTYPE_F32) -> Tensor:
@@ -265,6 +278,15 @@ class CudaBackend:
     # --- beyond the trait --------------------------------------------------------
     def argmax(self, stream: Stream, logits: Tensor) -> Tensor:
         return self._op(L.lib().beacon_cuda_op_argmax, stream.handle, logits.handle)
+
+    def profile_quantized_matmul(self, stream: Stream, weights, x: Tensor, iters: int = 10) -> tuple[float, int]:
+        """(mean microseconds per launch, algorithmic bytes per launch) of
+        quantized_matmul's decode path, cycling over `weights` (copies)."""
+        arr = (ctypes.c_void_p * len(weights))(*[w.handle.value for w in weights])
+        us, nb = ctypes.c_float(), ctypes.c_uint64()
+        _raise(L.lib().beacon_cuda_profile_quantized_matmul(self.ctx, stream.handle, arr, len(weights), x.handle,
+                                                            iters, ctypes.byref(us), ctypes.byref(nb)))
+        return us.value, nb.value
 
     def dequantize_to_f16(self, stream: Stream, w: Tensor) -> Tensor:
         return self._op(L.lib().beacon_cuda_op_dequantize_to_f16, stream.handle, w.handle)

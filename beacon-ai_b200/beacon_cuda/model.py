@@ -94,6 +94,11 @@ class CudaModel:
             self._h, s.handle, ctypes.c_void_p(d_tokens) if d_tokens else None, batch, position,
             ctypes.c_void_p(d_next) if d_next else None, ctypes.c_void_p(d_logits) if d_logits else None))
 
+    def synchronize(self, stream: Stream | None = None) -> None:
+        """Wait for the model's enqueued work; raises its device-side errors."""
+        s = stream or self.stream
+        _raise(L.lib().beacon_cuda_model_synchronize(self._h, s.handle))
+
     def profile_linear(self, slot: int, batch: int = 1, iters: int = 5) -> tuple[float, int]:
         """(mean microseconds per launch, algorithmic bytes per launch) of one projection."""
         us, nb = ctypes.c_float(), ctypes.c_uint64()

@@ -23,27 +23,33 @@ def _gen(seed: int, layer: int, slot: int):
     return g
 
 
-def quantized_tensor_on_device(model: CudaModel, n: int, k: int, dtype: int, seed: int, layer: int, slot: int,
-                               row_chunk: int = 8192):
-    """N(0, 0.02) [n, k] -> GGUF blocks in a torch uint8 device buffer."""
+def quantize_on_device(backend, stream, n: int, k: int, dtype: int, seed: int, layer: int, slot: int,
+                       row_chunk: int = 8192, scale: float = 0.02):
+    """N(0, scale) [n, k] -> GGUF blocks in a torch uint8 device buffer
+    (blocks along K, rows in order: the raw GGUF tensor bytes)."""
     import torch
     bs, bb = QUANT_BLOCK[dtype]
     out = torch.empty(n * (k // bs) * bb, dtype=torch.uint8, device="cuda")
     g = _gen(seed, layer, slot)
     row_bytes = k // bs * bb
-    stream = torch.cuda.current_stream()
     for r0 in range(0, n, row_chunk):
         r = min(row_chunk, n - r0)
-        x = torch.randn((r, k), generator=g, device="cuda", dtype=torch.float32).mul_(0.02)
+        x = torch.randn((r, k), generator=g, device="cuda", dtype=torch.float32).mul_(scale)
         torch.cuda.synchronize()
-        L.check(L.lib().beacon_cuda_quantize_blocks(model.backend.ctx, model.stream.handle,
+        L.check(L.lib().beacon_cuda_quantize_blocks(backend.ctx, stream.handle,
                                                     ctypes.c_void_p(x.data_ptr()), r, k, dtype,
                                                     L.NIBBLE_REF_INTERLEAVED,
                                                     ctypes.c_void_p(out.data_ptr() + r0 * row_bytes)))
-        model.stream.synchronize()
+        stream.synchronize()
         del x
-    stream.synchronize()
+    torch.cuda.synchronize()
     return out
+
+
+def quantized_tensor_on_device(model: CudaModel, n: int, k: int, dtype: int, seed: int, layer: int, slot: int,
+                               row_chunk: int = 8192):
+    """N(0, 0.02) [n, k] -> GGUF blocks in a torch uint8 device buffer."""
+    return quantize_on_device(model.backend, model.stream, n, k, dtype, seed, layer, slot, row_chunk)
 
 
 def load_synthetic(model: CudaModel, dtype: int, seed: int = 0) -> None:

@@ -102,7 +102,8 @@ __device__ __forceinline__ void attn_split_merge_bulk(const DecodeAttnArgs& a, i
     const bool ok = mbar_wait_bounded(&mbar, 0);
     if (__syncthreads_or(!ok)) {
         if (tid == 0) {
-            atomicExch(a.err, 3);
+            mbar_drain(&mbar, 0);  // the partial sums' copy must land before the CTA exits
+            atomicExch(a.err, kErrAttnWait);
             a.counters[bk] = 0;
         }
         return;
@@ -402,8 +403,8 @@ __device__ __forceinline__ void attn_unit(const DecodeAttnArgs& a, int bk, int s
     if (failed) {
         // let the copies still in flight land before the CTA exits
         for (int s2 = s; s2 < nsteps && s2 < s + kAttStages; ++s2)
-            mbar_wait_bounded(&bars[s2 % kAttStages], (uint32_t)((s2 / kAttStages) & 1));
-        if (tid == 0) atomicExch(a.err, 3);
+            mbar_drain(&bars[s2 % kAttStages], (uint32_t)((s2 / kAttStages) & 1));
+        if (tid == 0) atomicExch(a.err, kErrAttnWait);
         return;
     }
     // merge the warps (the ring is idle now)
@@ -641,8 +642,8 @@ __device__ __forceinline__ void attn_unit_tc(const DecodeAttnArgs& a, int bk, in
     }
     if (failed) {
         for (int s2 = s; s2 < nsteps && s2 < s + kTcStages; ++s2)
-            mbar_wait_bounded(&bars[s2 % kTcStages], (uint32_t)((s2 / kTcStages) & 1));
-        if (tid == 0) atomicExch(a.err, 3);
+            mbar_drain(&bars[s2 % kTcStages], (uint32_t)((s2 / kTcStages) & 1));
+        if (tid == 0) atomicExch(a.err, kErrAttnWait);
         return;
     }
     // combine the warps in warp order (the ring is idle now)

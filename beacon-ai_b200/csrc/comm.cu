@@ -20,28 +20,42 @@ static void nccl_check(ncclResult_t r, const char* what) {
         fail(BEACON_CUDA_ERR_COMM, std::string(what) + ": " + ncclGetErrorString(r));
 }
 
-// Wait until a non-blocking NCCL call has finished, at most timeout_ms.
-static void nccl_wait(ncclComm_t comm, int timeout_ms, const char* what) {
+// Wait until a non-blocking NCCL call has finished, at most timeout_ms. On an
+// error or a timeout the communicator is aborted (which frees it) and
+// `aborted` is called first, so no caller keeps a pointer to it.
+template <typename OnAbort>
+static void nccl_wait(ncclComm_t comm, int timeout_ms, const char* what, OnAbort&& aborted) {
     auto t0 = std::chrono::steady_clock::now();
+    auto abort_with = [&](const std::string& msg) {
+        aborted();
+        ncclCommAbort(comm);
+        fail(BEACON_CUDA_ERR_COMM, msg);
+    };
     for (;;) {
         ncclResult_t st = ncclSuccess;
         ncclResult_t r = ncclCommGetAsyncError(comm, &st);
-        if (r != ncclSuccess) nccl_check(r, what);
+        if (r != ncclSuccess) abort_with(std::string(what) + ": " + ncclGetErrorString(r));
         if (st == ncclSuccess) return;
-        if (st != ncclInProgress) {
-            ncclCommAbort(comm);
-            nccl_check(st, what);
-        }
+        if (st != ncclInProgress) abort_with(std::string(what) + ": " + ncclGetErrorString(st));
         const auto us =
             std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
-        if (us > (int64_t)timeout_ms * 1000) {
-            ncclCommAbort(comm);
-            fail(BEACON_CUDA_ERR_COMM, std::string(what) + ": timed out");
-        }
+        if (us > (int64_t)timeout_ms * 1000) abort_with(std::string(what) + ": timed out");
         // an enqueue finishes within microseconds; an initialisation takes longer
         if (us > 1000) std::this_thread::sleep_for(std::chrono::microseconds(200));
         else std::this_thread::yield();
     }
+}
+
+// The context's communicator, or an error if a failed collective aborted it.
+static ncclComm_t live_comm(BeaconCudaContext* ctx, const char* what) {
+    if (ctx->comm_aborted || !ctx->comm)
+        fail(BEACON_CUDA_ERR_COMM, std::string(what) + ": the communicator was aborted by an earlier failure");
+    return static_cast<ncclComm_t>(ctx->comm);
+}
+
+static void mark_aborted(BeaconCudaContext* ctx) {
+    ctx->comm = nullptr;
+    ctx->comm_aborted = true;
 }
 
 void comm_destroy(BeaconCudaContext* ctx) {
@@ -55,9 +69,14 @@ void comm_destroy(BeaconCudaContext* ctx) {
 // return ncclInProgress and must have finished enqueueing before the next one.
 void comm_all_reduce_sum(BeaconCudaContext* ctx, float* buf, size_t count, cudaStream_t s) {
     if (ctx->nranks <= 1) return;
-    ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
-    nccl_check(ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
-    nccl_wait(comm, ctx->comm_timeout_ms, "ncclAllReduce");
+    ncclComm_t comm = live_comm(ctx, "ncclAllReduce");
+    const ncclResult_t r = ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, comm, s);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        mark_aborted(ctx);
+        ncclCommAbort(comm);
+        nccl_check(r, "ncclAllReduce");
+    }
+    nccl_wait(comm, ctx->comm_timeout_ms, "ncclAllReduce", [&] { mark_aborted(ctx); });
 }
 
 void comm_all_gather(BeaconCudaContext* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
@@ -65,9 +84,14 @@ void comm_all_gather(BeaconCudaContext* ctx, const float* send, float* recv, siz
         if (send != recv) BC_CUDA(cudaMemcpyAsync(recv, send, count * 4, cudaMemcpyDeviceToDevice, s));
         return;
     }
-    ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
-    nccl_check(ncclAllGather(send, recv, count, ncclFloat32, comm, s), "ncclAllGather");
-    nccl_wait(comm, ctx->comm_timeout_ms, "ncclAllGather");
+    ncclComm_t comm = live_comm(ctx, "ncclAllGather");
+    const ncclResult_t r = ncclAllGather(send, recv, count, ncclFloat32, comm, s);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        mark_aborted(ctx);
+        ncclCommAbort(comm);
+        nccl_check(r, "ncclAllGather");
+    }
+    nccl_wait(comm, ctx->comm_timeout_ms, "ncclAllGather", [&] { mark_aborted(ctx); });
 }
 
 }  // namespace bc
@@ -93,6 +117,7 @@ int32_t beacon_cuda_comm_init(BeaconCudaContext* ctx, int32_t nranks, int32_t ra
         require(ctx && id_128, "comm_init: null argument");
         if (nranks < 1 || rank < 0 || rank >= nranks) invalid("comm_init: bad rank / nranks");
         if (ctx->comm) invalid("comm_init: context already has a communicator");
+        if (ctx->comm_aborted) fail(BEACON_CUDA_ERR_COMM, "comm_init: this context's communicator was aborted");
         set_device(ctx);
         ctx->comm_timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
         if (nranks == 1) {
@@ -106,7 +131,8 @@ int32_t beacon_cuda_comm_init(BeaconCudaContext* ctx, int32_t nranks, int32_t ra
         cfg.blocking = 0;
         ncclComm_t comm = nullptr;
         nccl_check(ncclCommInitRankConfig(&comm, nranks, id, rank, &cfg), "ncclCommInitRankConfig");
-        nccl_wait(comm, ctx->comm_timeout_ms, "ncclCommInitRankConfig");
+        // on failure the half-made communicator is aborted here and never stored
+        nccl_wait(comm, ctx->comm_timeout_ms, "ncclCommInitRankConfig", [] {});
         ctx->comm = comm;
         ctx->nranks = nranks;
         ctx->rank = rank;

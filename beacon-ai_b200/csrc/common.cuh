@@ -128,8 +128,40 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
 }
 
 // Shared-memory barriers and 1-D bulk copies (cp.async.bulk). Every wait is
-// bounded: after ~2^31 clock cycles it gives up and reports failure.
+// bounded. Two kinds:
+//  * mbar_wait_bounded: a wait the kernel's progress depends on (a tile copy,
+//    another warp's arrival). It gives up after g_wait_limit SM clock cycles
+//    (default 2^31, about 1.1 s at 1965 MHz), a per-device runtime value
+//    (beacon_cuda_context_set_wait_limit); the caller records an error and
+//    winds down.
+//  * mbar_drain: a wait for work this CTA itself already issued (copies into
+//    its shared memory, MMAs into its tensor memory) before the CTA may exit
+//    or release that memory. That work always completes, so the drain keeps
+//    the fixed long limit even when the runtime limit is shortened.
 constexpr long long kBoundedWaitLimit = 1LL << 31;
+
+// One copy per translation unit (internal linkage); every copy registers a
+// setter at load time so the runtime can update all of them for a device.
+static __device__ long long g_wait_limit = kBoundedWaitLimit;
+void register_wait_limit_setter(cudaError_t (*setter)(long long));
+namespace {
+cudaError_t set_wait_limit_here(long long cycles) {
+    return cudaMemcpyToSymbol(g_wait_limit, &cycles, sizeof(cycles));
+}
+struct WaitLimitRegistration {
+    WaitLimitRegistration() { register_wait_limit_setter(&set_wait_limit_here); }
+};
+const WaitLimitRegistration g_wait_limit_registration;
+}  // namespace
+
+// Error codes written by kernels to an error word (0 = none).
+enum DeviceErr : int {
+    kErrTokenRange = 1,    // a token id outside the vocabulary
+    kErrContext = 2,       // a device-advanced position ran past the KV cache
+    kErrAttnWait = 3,      // decode attention: a bounded wait gave up
+    kErrGemmWait = 4,      // tensor-core GEMM: a bounded pipeline wait gave up
+    kErrGemvWait = 5,      // persistent GEMV: a bounded wait gave up
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -167,8 +199,19 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* ptr, int v) {
     return old;
 }
 
-// Bounded wait; false if the limit was reached.
+// Bounded wait on progress; false if the runtime limit was reached.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long limit = *(volatile long long*)&g_wait_limit;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > limit) return false;
+    return true;
+}
+
+// Bounded wait for this CTA's own issued work; false only after the fixed
+// long limit.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity))
         if (clock64() - t0 > kBoundedWaitLimit) return false;

@@ -469,7 +469,7 @@ __device__ __forceinline__ void gemv_store(const GemvParams& p, int epi, int64_t
             const int rr = e.row0 + b;
             const int pos = pos0 + rr * e.pos_step;
             if (pos < 0 || pos >= e.max_ctx) {  // a device-advanced position ran past the cache
-                atomicExch(e.err, 2);
+                atomicExch(e.err, kErrContext);
                 continue;
             }
             const int64_t cache_at = (int64_t)rr * e.seq_step * e.cache_sb + (int64_t)pos * e.kd;

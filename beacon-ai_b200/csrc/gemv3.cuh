@@ -21,8 +21,8 @@
 //  * programmatic dependent launch: the first S tiles of every warp are
 //    requested before waiting on the previous kernel (weights are never
 //    written), so the weight stream overlaps the previous kernel's tail.
-// Every mbarrier wait is bounded: after ~2^31 clock cycles the warp records
-// an error, waits (again bounded) for its own copies still in flight, and
+// Every mbarrier wait is bounded: after the runtime limit the warp records
+// an error (kErrGemvWait), drains its own copies still in flight, and
 // returns.
 #pragma once
 
@@ -42,7 +42,7 @@ struct Gemv3Params {
     int kspan;            // staged activation columns (k_pad)
     float* slots;         // [CTAs][2][B][32] partial sums of the CTAs' first and last groups
     int* counters;        // [groups], zero at rest
-    int* err;             // set to 1 when a wait gives up
+    int* err;             // set to kErrGemvWait when a wait gives up
 };
 
 // Staging of the activations. Thread t of pass i covers columns
@@ -523,7 +523,12 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             t = warp_sum(t);
             if (lane == 0) inv_s[warp] = 1.0f / sqrtf(t / (float)p.k + p.norm_eps);
         }
-        if (!mbar_wait_bounded(&qx_bar, 0) && lane == 0) atomicExch(a.err, 1);
+        if (!mbar_wait_bounded(&qx_bar, 0)) {
+            if (threadIdx.x == 0) {
+                atomicExch(a.err, kErrGemvWait);
+                mbar_drain(&qx_bar, 0);  // the image copy must land before the CTA exits
+            }
+        }
     } else {
         stage_x_full<FMT, MODE, B>(p, xs, a.kspan, nwr);
     }
@@ -569,9 +574,9 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
         }
     }
     if (!ok) {
-        if (lane == 0) atomicExch(a.err, 1);
+        if (lane == 0) atomicExch(a.err, kErrGemvWait);
         // let this warp's copies still in flight land before the CTA exits
-        for (int j = i; j < n && j < i + S; ++j) mbar_wait_bounded(&mybar[j % S], (uint32_t)((j / S) & 1));
+        for (int j = i; j < n && j < i + S; ++j) mbar_drain(&mybar[j % S], (uint32_t)((j / S) & 1));
     }
 }
 

@@ -180,17 +180,17 @@ void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, cons
     }
 }
 
-GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const LinearPlan& pl, int batch, const QLayout& L,
-                                 cudaStream_t s) {
+GemvScratch stream_gemv_scratch(BeaconCudaStream* stream, const LinearPlan& pl, int batch, const QLayout& L) {
     GemvScratch sc;
+    Workspace& ws = stream->ws;
     const size_t pf = pl.scratch_floats(batch, L);
-    ctx->ws.get(pf * sizeof(float), s);  // grows (and zeroes) the arena when needed
-    sc.err = ctx->ws.flags() + 1;
+    void* data = ws.get(pf * sizeof(float), stream->s);  // grows (and zeroes) the arena when needed
+    sc.err = ws.flags() + Workspace::kTimeoutFlag;
     if (pf == 0) return sc;
     if ((size_t)L.groups() > Workspace::kCounterInts) shape_err("too many rows for the split-K counters");
-    sc.partial = static_cast<float*>(ctx->ws.get(pf * sizeof(float), s));
+    sc.partial = static_cast<float*>(data);
     sc.partial_floats = pf;
-    sc.counters = ctx->ws.counters();
+    sc.counters = ws.counters();
     sc.counter_count = (int64_t)Workspace::kCounterInts;
     return sc;
 }
@@ -198,22 +198,23 @@ GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const LinearPlan& pl, i
 // Prefill-sized matmul: the tensor-core GEMM in the fast numerics, otherwise
 // the GEMV in 16-row chunks (each chunk streams the weight once), which
 // follows the exact and CPU-reproducing numerics to the bit.
-void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTensor* w, const void* x, bool x_f16,
-                   int64_t rows, float* out, int numerics) {
+void dense_qmatmul(BeaconCudaContext* ctx, BeaconCudaStream* stream, const BeaconCudaTensor* w, const void* x,
+                   bool x_f16, int64_t rows, float* out, int numerics) {
     const int mode = numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32;
     const bool rtz = numerics == BEACON_CUDA_NUMERICS_REF_RTZ;
     const QLayout& L = w->q;
     const size_t eb = x_f16 ? 2 : 4;
+    cudaStream_t s = stream->s;
     if (mode == MODE_FAST && qgemm_tc_supported(L)) {
-        void* x16 = ctx->ws.get(qgemm_tc_scratch_bytes(rows, L.k), s);
-        launch_qgemm_tc(L, w->data(), x, x_f16, L.k, rows, out, L.n, EPI_STORE, nullptr, 0, false, ctx->ws.flags() + 1, s,
-                        x16);
+        void* x16 = stream->ws.get(qgemm_tc_scratch_bytes(rows, L.k), s);
+        launch_qgemm_tc(L, w->data(), x, x_f16, L.k, rows, out, L.n, EPI_STORE, nullptr, 0, false,
+                        stream->ws.flags() + Workspace::kTimeoutFlag, s, x16);
         return;
     }
     for (int64_t r0 = 0; r0 < rows; r0 += 16) {
         const int b = (int)std::min<int64_t>(16, rows - r0);
         LinearPlan pl = plan_linear(ctx, L, b, mode);
-        GemvScratch sc = context_gemv_scratch(ctx, pl, b, L, s);
+        GemvScratch sc = stream_gemv_scratch(stream, pl, b, L);
         launch_linear(pl, L, w->data(), static_cast<const uint8_t*>(x) + (size_t)r0 * L.k * eb, x_f16, L.k, b,
                       out + r0 * L.n, L.n, EPI_STORE, nullptr, 0, mode, rtz, sc, s);
     }

@@ -6,6 +6,8 @@
 
 #include <cstdint>
 #include <memory>
+#include <mutex>
+#include <set>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -113,19 +115,25 @@ struct DeviceBuffer {
     DeviceBuffer& operator=(const DeviceBuffer&) = delete;
 };
 
-// Grow-only scratch arena of a context. Layout: [counters | flags | data].
+// Grow-only scratch arena of one stream. Layout: [counters | flags | data].
 // The split-K arrival counters sit at a fixed offset and are zero whenever no
 // kernel is running (each launch resets the ones it used), so data written
-// by one op can never be mistaken for counters by the next. Grown outside
-// captured regions; never shrinks while the context lives.
+// by one op can never be mistaken for counters by the next. Each stream has
+// its own, so ops on different streams of a context never share scratch.
+// Growing is refused during stream capture, and a replaced buffer is kept
+// (not freed) until the stream is destroyed, so work already enqueued -- or a
+// graph captured earlier -- never touches freed memory.
 struct Workspace {
     static constexpr size_t kCounterInts = 1 << 16;  // one per 32-row group: 2M rows
     static constexpr size_t kFlagInts = 64;
     static constexpr size_t kDataOffset = (kCounterInts + kFlagInts) * sizeof(int);
     std::unique_ptr<DeviceBuffer> buf;
+    std::vector<std::unique_ptr<DeviceBuffer>> retired;
     void* get(size_t data_bytes, cudaStream_t s);  // returns the data region
     int* counters() const { return static_cast<int*>(buf->ptr); }
     int* flags() const { return static_cast<int*>(buf->ptr) + kCounterInts; }
+    // flags()[kTimeoutFlag]: a bounded device wait of an op on this stream gave up
+    static constexpr int kTimeoutFlag = 1;
 };
 
 }  // namespace bc
@@ -134,10 +142,14 @@ struct BeaconCudaContext {
     int device = 0;
     int sm_count = 148;
     int32_t numerics = BEACON_CUDA_NUMERICS_FAST;
-    bc::Workspace ws;
     cudaStream_t internal = nullptr;  // uploads and frees outside any user stream
+    // streams made on this context (their workspaces are checked for device
+    // timeouts at the context-wide synchronisation points)
+    std::mutex streams_mu;
+    std::set<BeaconCudaStream*> streams;
     // tensor parallelism
     void* comm = nullptr;  // ncclComm_t
+    bool comm_aborted = false;  // a failed or timed-out collective aborted the communicator
     int nranks = 1, rank = 0;
     int comm_timeout_ms = 60000;
 };
@@ -146,6 +158,7 @@ struct BeaconCudaStream {
     BeaconCudaContext* ctx = nullptr;
     cudaStream_t s = nullptr;
     bool owned = false;
+    bc::Workspace ws;  // split-K scratch, arrival counters and error flags of ops on this stream
 };
 
 struct BeaconCudaTensor {
@@ -172,5 +185,13 @@ BeaconCudaTensor* view_tensor(const BeaconCudaTensor* base, const std::vector<in
                               size_t byte_offset, int32_t dtype);
 void set_device(BeaconCudaContext* ctx);
 inline cudaStream_t stream_of(BeaconCudaStream* s) { return s ? s->s : nullptr; }
+
+// After the stream (or the whole device) has been synchronised: if a bounded
+// device wait of an op on this stream gave up, clear the flag, re-zero the
+// stream's arrival counters (a warp that gave up never arrived) and throw
+// BEACON_CUDA_ERR_DEVICE_TIMEOUT.
+void check_stream_timeout(BeaconCudaStream* stream);
+// The same for every stream of the context (after a device synchronisation).
+void check_context_timeouts(BeaconCudaContext* ctx);
 
 }  // namespace bc

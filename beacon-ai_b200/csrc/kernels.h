@@ -168,13 +168,12 @@ void launch_dequant_f16(const QLayout& L, const uint8_t* tiled, uint16_t* out, c
 void launch_quantize(int32_t dtype, const float* x, int64_t n_rows, int64_t k, int nibble_order,
                      uint8_t* raw, cudaStream_t s);
 
-// Split-K scratch carved from the context workspace (fixed zeroed counters).
+// Split-K scratch carved from the stream's workspace (fixed zeroed counters).
 struct LinearPlan;
-GemvScratch context_gemv_scratch(BeaconCudaContext* ctx, const LinearPlan& pl, int batch, const QLayout& L,
-                                 cudaStream_t s);
+GemvScratch stream_gemv_scratch(BeaconCudaStream* stream, const LinearPlan& pl, int batch, const QLayout& L);
 
 // Prefill-sized quantized matmul (rows > 16): out[rows, N] = x @ W^T.
-void dense_qmatmul(BeaconCudaContext* ctx, cudaStream_t s, const BeaconCudaTensor* w, const void* x,
+void dense_qmatmul(BeaconCudaContext* ctx, BeaconCudaStream* stream, const BeaconCudaTensor* w, const void* x,
                    bool x_f16, int64_t rows, float* out, int numerics);
 
 // Tensor parallelism (comm.cu).

@@ -48,7 +48,7 @@ __global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hi
     const int row = blockIdx.x;
     const int32_t t = tok[row];
     const bool ok = t >= 0 && t < vocab;
-    if (!ok && threadIdx.x == 0) atomicExch(err, 1);
+    if (!ok && threadIdx.x == 0) atomicExch(err, kErrTokenRange);
     for (int64_t i = threadIdx.x; i < hid; i += blockDim.x) {  // warp-uniform when hid % 32 == 0
         float v = 0.0f;
         if (ok) v = e_f16 ? __half2float(static_cast<const __half*>(E)[(int64_t)t * hid + i])
@@ -194,6 +194,7 @@ struct BeaconCudaModel {
     int attn_nsplit = 1;
     float *pacc = nullptr, *pm = nullptr, *pl = nullptr;
     int* attn_cnt = nullptr;
+    size_t attn_cnt_count = 0;
     std::unique_ptr<bc::DeviceBuffer> argmax_buf;
     bool pdl = true;  // programmatic dependent launch between the step's kernels
     bc::ArgmaxSummary* argmax_scratch = nullptr;
@@ -477,17 +478,29 @@ void check_ready(const BeaconCudaModel* m) {
         if (m->layers[i].set != layer_all) invalid("model: layer " + std::to_string(i) + " has unset weights");
 }
 
+// Reads the model's error word after the stream's work (synchronises). A
+// bounded wait that gave up leaves arrival counters of the warps that never
+// arrived: they are re-zeroed, so the next step starts clean.
 void check_err(BeaconCudaModel* m, cudaStream_t s) {
     int herr = 0;
     BC_CUDA(cudaMemcpyAsync(&herr, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s));
     BC_CUDA(cudaStreamSynchronize(s));
-    if (herr) {
-        BC_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), s));
-        if (herr == 2) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
-        if (herr == 3) fail(BEACON_CUDA_ERR_CUDA, "decode attention: a bounded wait for the KV cache copies gave up");
-        if (herr == 4) fail(BEACON_CUDA_ERR_CUDA, "tensor-core GEMM: a bounded pipeline wait gave up");
-        shape_err("token id out of range for the vocabulary");
+    if (!herr) return;
+    BC_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), s));
+    if (herr == kErrAttnWait || herr == kErrGemmWait || herr == kErrGemvWait) {
+        if (m->gsc.counters)
+            BC_CUDA(cudaMemsetAsync(m->gsc.counters, 0, (size_t)m->gsc.counter_count * sizeof(int), s));
+        if (m->attn_cnt)
+            BC_CUDA(cudaMemsetAsync(m->attn_cnt, 0, (size_t)m->attn_cnt_count * sizeof(int), s));
+        BC_CUDA(cudaStreamSynchronize(s));
+        const char* what = herr == kErrAttnWait   ? "decode attention: a bounded wait for its copies gave up"
+                           : herr == kErrGemmWait ? "tensor-core GEMM: a bounded pipeline wait gave up"
+                                                  : "dequant-GEMV: a bounded wait for its weight tiles gave up";
+        fail(BEACON_CUDA_ERR_DEVICE_TIMEOUT, std::string(what) + "; the step's outputs are invalid");
     }
+    BC_CUDA(cudaStreamSynchronize(s));
+    if (herr == kErrContext) fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
+    shape_err("token id out of range for the vocabulary");
 }
 
 // Copy the raw GGUF bytes of rows [r0, r0+nr) and columns [c0, c0+nc) of a
@@ -663,6 +676,7 @@ int32_t beacon_cuda_model_create(BeaconCudaContext* ctx, const BeaconCudaModelCo
         m->pm = m->pacc + pa * c.head_dim;
         m->pl = m->pm + pa;
         m->attn_cnt = reinterpret_cast<int*>(m->pl + pa);
+        m->attn_cnt_count = ncnt;
         BC_CUDA(cudaMemset(m->attn_cnt, 0, ncnt * 4));
         if (tp == 1 && c.hidden_size % 32 == 0) {
             const int64_t kh = (c.hidden_size + 255) / 256 * 256, ka = (m->qd + 255) / 256 * 256,
@@ -837,7 +851,7 @@ int32_t beacon_cuda_model_set_weight(BeaconCudaModel* m, int32_t layer, int32_t 
             m->gsc.partial_floats = pf;
             m->gsc.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(m->gemv_buf->ptr) + coff);
             m->gsc.counter_count = (int64_t)cc;
-            m->gsc.err = reinterpret_cast<int*>(static_cast<uint8_t*>(m->gemv_buf->ptr) + coff + cc * 4);
+            m->gsc.err = m->err_dev;  // GEMV timeouts surface through check_err like every other device error
         }
         return BEACON_CUDA_OK;
     });
@@ -970,7 +984,7 @@ int32_t beacon_cuda_model_decode_step(BeaconCudaModel* m, BeaconCudaStream* stre
         if (next_tokens) BC_CUDA(cudaMemcpyAsync(m->h_next, m->next, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
         if (logits_out)
             BC_CUDA(cudaMemcpyAsync(logits_out, full_logits(m), (size_t)batch * c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
-        BC_CUDA(cudaStreamSynchronize(s));
+        check_err(m, s);  // synchronises the stream
         if (next_tokens)
             for (int i = 0; i < batch; ++i) next_tokens[i] = (uint32_t)m->h_next[i];
         return BEACON_CUDA_OK;
@@ -1002,6 +1016,15 @@ int32_t beacon_cuda_model_decode_step_device(BeaconCudaModel* m, BeaconCudaStrea
         if (d_next_tokens) BC_CUDA(cudaMemcpyAsync(d_next_tokens, m->next, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
         if (d_logits)
             BC_CUDA(cudaMemcpyAsync(d_logits, full_logits(m), (size_t)batch * c.vocab_size * 4, cudaMemcpyDeviceToDevice, s));
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_synchronize(BeaconCudaModel* m, BeaconCudaStream* stream) {
+    return guard([&]() -> int32_t {
+        require(m && stream, "model_synchronize: null argument");
+        set_device(m->ctx);
+        check_err(m, stream->s);
         return BEACON_CUDA_OK;
     });
 }

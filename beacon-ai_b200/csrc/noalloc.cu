@@ -66,6 +66,7 @@ extern "C" int32_t beacon_cuda_quantized_matvec_noalloc(BeaconCudaStream* stream
             fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized_matvec_noalloc: x must be F32 or F16");
         if (batch < 1 || batch > 16) invalid("quantized_matvec_noalloc: batch must be 1..16");
         BeaconCudaContext* ctx = w->ctx;
+        require(stream->ctx == ctx, "quantized_matvec_noalloc: the stream belongs to another context than w");
         set_device(ctx);
         const QLayout& L = w->q;
         const int mode = ctx->numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32;

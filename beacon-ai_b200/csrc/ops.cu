@@ -178,6 +178,7 @@ template <typename F>
 int32_t op_guard(BeaconCudaContext* ctx, BeaconCudaStream* stream, BeaconCudaTensor** out, F&& body) {
     return guard([&]() -> int32_t {
         require(ctx && stream && out, "null context, stream or output");
+        if (stream->ctx != ctx) invalid("the stream belongs to another context");
         set_device(ctx);
         *out = body();
         return BEACON_CUDA_OK;
@@ -378,8 +379,8 @@ int32_t beacon_cuda_op_embedding(BeaconCudaContext* ctx, BeaconCudaStream* strea
             fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "embedding: indices must be I32 or F32");
         const int64_t vocab = weight->shape[0], h = weight->shape[1], seq = indices->numel();
         TensorHolder o(new_tensor(ctx, {seq, h}, BEACON_CUDA_DTYPE_F32));
-        ctx->ws.get(0, stream->s);
-        int* err = ctx->ws.flags();
+        stream->ws.get(0, stream->s);
+        int* err = stream->ws.flags();
         BC_CUDA(cudaMemsetAsync(err, 0, sizeof(int), stream->s));
         if (seq)
             embedding_kernel<<<(unsigned)seq, 256, 0, stream->s>>>(weight->data(), weight->dtype, vocab, h,
@@ -455,7 +456,7 @@ int32_t beacon_cuda_op_argmax(BeaconCudaContext* ctx, BeaconCudaStream* stream, 
             BC_CUDA(cudaMemsetAsync(o.t->data(), 0, (size_t)rows * 4, stream->s));  // empty -> 0 (sampling.rs:65)
         } else if (rows) {
             auto* scratch = static_cast<ArgmaxSummary*>(
-                ctx->ws.get(argmax_scratch_count(d, 1, (int)rows) * sizeof(ArgmaxSummary), stream->s));
+                stream->ws.get(argmax_scratch_count(d, 1, (int)rows) * sizeof(ArgmaxSummary), stream->s));
             launch_argmax(static_cast<const float*>(logits->data()), d, 1, (int)rows,
                           static_cast<int32_t*>(o.t->data()), nullptr, scratch, stream->s);
         }

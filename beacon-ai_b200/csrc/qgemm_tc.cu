@@ -254,7 +254,7 @@ __device__ __forceinline__ void tc_epilogue32(const TcParams& p, int64_t m, int6
         const int rr = e.row0 + (int)m;
         const int pos = (e.pos_ptr ? *e.pos_ptr : e.pos_imm) + rr * e.pos_step;
         if (pos < 0 || pos >= e.max_ctx) {
-            atomicExch(e.err, 2);
+            atomicExch(e.err, kErrContext);
             return;
         }
         const int64_t cache_at = (int64_t)rr * e.seq_step * e.cache_sb + (int64_t)pos * e.kd;
@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
             const int s = kb % kTcStages;
             if (live && kb + 1 < nkb) load_slice<FMT>(p, wrow, kb + 1, bh, nxt);  // in flight while this slice converts
             if (kb >= kTcStages && !mbar_wait_bounded(&empty_bar[s], (uint32_t)((kb / kTcStages - 1) & 1))) {
-                atomicExch(p.err, 4);
+                atomicExch(p.err, kErrGemmWait);
                 failed_s = 1;
                 break;
             }
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kTcStages;
                 if (kb >= kTcStages && !mbar_wait_bounded(&empty_bar[s], (uint32_t)((kb / kTcStages - 1) & 1))) {
-                    atomicExch(p.err, 4);
+                    atomicExch(p.err, kErrGemmWait);
                     failed_s = 1;
                     break;
                 }
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
             }
             // no copy may still be landing when the CTA exits
             for (int kb = issued - 1; kb >= 0 && kb >= issued - kTcStages; --kb)
-                mbar_wait_bounded(&aload_bar[kb % kTcStages], (uint32_t)((kb / kTcStages) & 1));
+                mbar_drain(&aload_bar[kb % kTcStages], (uint32_t)((kb / kTcStages) & 1));
         }
     } else if (lane == 0) {
         // MMA issuer: both 128-row halves against the same weight slice
@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
             const int s = kb % kTcStages;
             if (!mbar_wait_bounded(&aload_bar[s], (uint32_t)((kb / kTcStages) & 1)) ||
                 !mbar_wait_bounded(&full_bar[s], (uint32_t)((kb / kTcStages) & 1)) || failed_s) {
-                atomicExch(p.err, 4);
+                atomicExch(p.err, kErrGemmWait);
                 failed_s = 1;
                 break;
             }
@@ -431,8 +431,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
     // epilogue: warp w owns accumulator lanes 32 (w % 4) .. + 31 of row half
     // (w / 4) % 2, columns 128 (w / 8) .. + 127
     if (warp < kTcProducerWarps) {
-        const bool ok = mbar_wait_bounded(&done_bar, 0);
-        if (!ok) atomicExch(p.err, 4);
+        // every issued MMA completes: wait for them before TMEM is read or freed
+        const bool ok = mbar_drain(&done_bar, 0);
+        if (!ok) atomicExch(p.err, kErrGemmWait);
         tc_fence_after();
         if (ok && !failed_s && nkb > 0) {
             const int q = warp & 3, h = (warp >> 2) & 1, cb = (warp >> 3) * (kTcBN / 2);

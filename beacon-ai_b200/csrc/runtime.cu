@@ -102,13 +102,54 @@ void* Workspace::get(size_t data_bytes, cudaStream_t s) {
             if (st != cudaStreamCaptureStatusNone)
                 invalid("workspace must grow outside stream capture; run the op once before capturing");
         }
-        BC_CUDA(cudaDeviceSynchronize());
-        buf.reset();
         size_t want = std::max<size_t>(bytes, 1 << 20);
-        buf = std::make_unique<DeviceBuffer>(want);
-        BC_CUDA(cudaMemset(buf->ptr, 0, want));
+        if (buf) want = std::max(want, 2 * buf->bytes);
+        auto nb = std::make_unique<DeviceBuffer>(want);
+        // zeroed in stream order: earlier work on this stream keeps using the
+        // old buffer, which stays allocated until the stream is destroyed
+        BC_CUDA(cudaMemsetAsync(nb->ptr, 0, want, s));
+        if (buf) {
+            // carry the error flags over (an op that timed out before the
+            // growth must still be reported)
+            BC_CUDA(cudaMemcpyAsync(static_cast<int*>(nb->ptr) + kCounterInts,
+                                    static_cast<int*>(buf->ptr) + kCounterInts, kFlagInts * sizeof(int),
+                                    cudaMemcpyDeviceToDevice, s));
+            retired.push_back(std::move(buf));
+        }
+        buf = std::move(nb);
     }
     return static_cast<uint8_t*>(buf->ptr) + kDataOffset;
+}
+
+// Setters of the per-translation-unit copies of the device wait limit.
+static std::vector<cudaError_t (*)(long long)>& wait_limit_setters() {
+    static std::vector<cudaError_t (*)(long long)> v;
+    return v;
+}
+void register_wait_limit_setter(cudaError_t (*setter)(long long)) { wait_limit_setters().push_back(setter); }
+
+void check_stream_timeout(BeaconCudaStream* stream) {
+    if (!stream || !stream->ws.buf) return;
+    if (stream->ctx) set_device(stream->ctx);
+    int flag = 0;
+    BC_CUDA(cudaMemcpy(&flag, stream->ws.flags() + Workspace::kTimeoutFlag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (!flag) return;
+    BC_CUDA(cudaDeviceSynchronize());
+    BC_CUDA(cudaMemset(stream->ws.flags() + Workspace::kTimeoutFlag, 0, sizeof(int)));
+    BC_CUDA(cudaMemset(stream->ws.counters(), 0, Workspace::kCounterInts * sizeof(int)));
+    BC_CUDA(cudaDeviceSynchronize());
+    fail(BEACON_CUDA_ERR_DEVICE_TIMEOUT,
+         "a bounded device-side wait gave up (code " + std::to_string(flag) +
+             "); the op's output is invalid. The stream's scratch counters were reset");
+}
+
+void check_context_timeouts(BeaconCudaContext* ctx) {
+    std::vector<BeaconCudaStream*> ss;
+    {
+        std::lock_guard<std::mutex> lk(ctx->streams_mu);
+        ss.assign(ctx->streams.begin(), ctx->streams.end());
+    }
+    for (BeaconCudaStream* st : ss) check_stream_timeout(st);
 }
 
 void set_device(BeaconCudaContext* ctx) { BC_CUDA(cudaSetDevice(ctx->device)); }
@@ -228,10 +269,28 @@ void beacon_cuda_context_destroy(BeaconCudaContext* ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
-    ctx->ws.buf.reset();
+    {
+        // streams outliving their context keep their handles but lose the link
+        std::lock_guard<std::mutex> lk(ctx->streams_mu);
+        for (BeaconCudaStream* st : ctx->streams) st->ctx = nullptr;
+        ctx->streams.clear();
+    }
     if (ctx->internal) cudaStreamDestroy(ctx->internal);
     comm_destroy(ctx);
     delete ctx;
+}
+
+int32_t beacon_cuda_context_set_wait_limit(BeaconCudaContext* ctx, int64_t cycles) {
+    return guard([&]() -> int32_t {
+        require(ctx != nullptr, "null context");
+        if (cycles < 0) invalid("set_wait_limit: the limit must be >= 0 clock cycles (0 restores the default)");
+        set_device(ctx);
+        BC_CUDA(cudaDeviceSynchronize());
+        const long long v = cycles == 0 ? kBoundedWaitLimit : (long long)cycles;
+        for (auto setter : wait_limit_setters()) BC_CUDA(setter(v));
+        BC_CUDA(cudaDeviceSynchronize());
+        return BEACON_CUDA_OK;
+    });
 }
 
 int32_t beacon_cuda_context_set_numerics(BeaconCudaContext* ctx, int32_t numerics) {
@@ -252,6 +311,10 @@ int32_t beacon_cuda_stream_create(BeaconCudaContext* ctx, BeaconCudaStream** out
         s->ctx = ctx;
         s->owned = true;
         BC_CUDA(cudaStreamCreateWithFlags(&s->s, cudaStreamNonBlocking));
+        {
+            std::lock_guard<std::mutex> lk(ctx->streams_mu);
+            ctx->streams.insert(s.get());
+        }
         *out_stream = s.release();
         return BEACON_CUDA_OK;
     });
@@ -264,6 +327,10 @@ int32_t beacon_cuda_stream_wrap(BeaconCudaContext* ctx, void* cuda_stream, Beaco
         s->ctx = ctx;
         s->owned = false;
         s->s = static_cast<cudaStream_t>(cuda_stream);
+        {
+            std::lock_guard<std::mutex> lk(ctx->streams_mu);
+            ctx->streams.insert(s.get());
+        }
         *out_stream = s.release();
         return BEACON_CUDA_OK;
     });
@@ -271,10 +338,12 @@ int32_t beacon_cuda_stream_wrap(BeaconCudaContext* ctx, void* cuda_stream, Beaco
 
 void beacon_cuda_stream_destroy(BeaconCudaStream* stream) {
     if (!stream) return;
-    if (stream->owned && stream->s) {
-        cudaStreamSynchronize(stream->s);
-        cudaStreamDestroy(stream->s);
+    if (stream->ctx) {
+        std::lock_guard<std::mutex> lk(stream->ctx->streams_mu);
+        stream->ctx->streams.erase(stream);
     }
+    if (stream->s) cudaStreamSynchronize(stream->s);  // its workspace may still be in use
+    if (stream->owned && stream->s) cudaStreamDestroy(stream->s);
     delete stream;
 }
 
@@ -282,6 +351,7 @@ int32_t beacon_cuda_stream_synchronize(BeaconCudaStream* stream) {
     return guard([&]() -> int32_t {
         require(stream != nullptr, "null stream");
         BC_CUDA(cudaStreamSynchronize(stream->s));
+        check_stream_timeout(stream);
         return BEACON_CUDA_OK;
     });
 }
@@ -398,10 +468,14 @@ int32_t beacon_cuda_tensor_device_ptr(const BeaconCudaTensor* t, void** out_ptr)
 int32_t beacon_cuda_tensor_eval(BeaconCudaTensor* t, BeaconCudaStream* stream) {
     return guard([&]() -> int32_t {
         require(t != nullptr, "beacon_cuda_tensor_eval: null tensor");
-        if (stream)
+        if (stream) {
             BC_CUDA(cudaStreamSynchronize(stream->s));
-        else
+            check_stream_timeout(stream);
+        } else {
+            set_device(t->ctx);
             BC_CUDA(cudaDeviceSynchronize());
+            check_context_timeouts(t->ctx);
+        }
         return BEACON_CUDA_OK;
     });
 }
@@ -412,6 +486,7 @@ int32_t beacon_cuda_tensor_read_raw(const BeaconCudaTensor* t, void* out, size_t
         if (n_bytes > t->nbytes()) shape_err("read_raw: more bytes requested than the tensor holds");
         set_device(t->ctx);
         BC_CUDA(cudaDeviceSynchronize());
+        check_context_timeouts(t->ctx);
         BC_CUDA(cudaMemcpy(out, t->data(), n_bytes, cudaMemcpyDeviceToHost));
         return BEACON_CUDA_OK;
     });
@@ -425,6 +500,7 @@ int32_t beacon_cuda_tensor_read_f32(const BeaconCudaTensor* t, float* out, size_
         if (is_quantized(t->dtype)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "read_f32 of a quantized tensor");
         set_device(t->ctx);
         BC_CUDA(cudaDeviceSynchronize());
+        check_context_timeouts(t->ctx);
         const size_t eb = plain_elem_bytes(t->dtype);
         if (t->dtype == BEACON_CUDA_DTYPE_F32) {
             BC_CUDA(cudaMemcpy(out, t->data(), n_elements * 4, cudaMemcpyDeviceToHost));
@@ -491,12 +567,14 @@ int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream
         try {
             const int mode = ctx->numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32;
             const bool rtz = ctx->numerics == BEACON_CUDA_NUMERICS_REF_RTZ;
+            if (stream->ctx != ctx || w->ctx != ctx || x->ctx != ctx)
+                invalid("quantized_matmul: the stream and tensors must belong to the context");
             if (rows > 16) {
-                dense_qmatmul(ctx, stream->s, w, x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, rows,
+                dense_qmatmul(ctx, stream, w, x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, rows,
                               static_cast<float*>(o->data()), ctx->numerics);
             } else if (rows > 0) {
                 LinearPlan pl = plan_linear(ctx, w->q, (int)rows, mode);
-                GemvScratch sc = context_gemv_scratch(ctx, pl, (int)rows, w->q, stream->s);
+                GemvScratch sc = stream_gemv_scratch(stream, pl, (int)rows, w->q);
                 launch_linear(pl, w->q, w->data(), x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, K, (int)rows,
                               static_cast<float*>(o->data()), w->q.n, EPI_STORE, nullptr, 0, mode, rtz, sc,
                               stream->s);
@@ -506,6 +584,57 @@ int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream
             throw;
         }
         *out = o;
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_profile_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                             const BeaconCudaTensor* const* w, int32_t n_w,
+                                             const BeaconCudaTensor* x, int32_t iters, float* out_avg_us,
+                                             uint64_t* out_bytes) {
+    return guard([&]() -> int32_t {
+        require(ctx && stream && w && x && out_avg_us && out_bytes, "profile_quantized_matmul: null argument");
+        require(n_w >= 1 && iters >= 1, "profile_quantized_matmul: need at least one weight and one iteration");
+        require(stream->ctx == ctx, "profile_quantized_matmul: the stream belongs to another context");
+        const QLayout& L0 = w[0]->q;
+        for (int i = 0; i < n_w; ++i) {
+            require(w[i] != nullptr && is_quantized(w[i]->dtype), "profile_quantized_matmul: w must be quantized");
+            if (w[i]->dtype != L0.dtype || w[i]->q.n != L0.n || w[i]->q.k != L0.k)
+                shape_err("profile_quantized_matmul: every weight must have the same block type and shape");
+        }
+        if (x->dtype != BEACON_CUDA_DTYPE_F32 && x->dtype != BEACON_CUDA_DTYPE_F16)
+            fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "profile_quantized_matmul: x must be F32 or F16");
+        if (x->shape.empty() || x->shape.back() != L0.k) shape_err("profile_quantized_matmul: inner dimension");
+        const int64_t rows = x->numel() / L0.k;
+        if (rows < 1 || rows > 16) invalid("profile_quantized_matmul: 1..16 activation rows");
+        set_device(ctx);
+        const int mode = ctx->numerics == BEACON_CUDA_NUMERICS_FAST ? MODE_FAST : MODE_F32;
+        const bool rtz = ctx->numerics == BEACON_CUDA_NUMERICS_REF_RTZ;
+        const bool x16 = x->dtype == BEACON_CUDA_DTYPE_F16;
+        DeviceBuffer y((size_t)rows * L0.n * 4);
+        LinearPlan pl = plan_linear(ctx, L0, (int)rows, mode);
+        GemvScratch sc = stream_gemv_scratch(stream, pl, (int)rows, L0);
+        auto round = [&]() {
+            for (int i = 0; i < n_w; ++i)
+                launch_linear(pl, L0, w[i]->data(), x->data(), x16, L0.k, (int)rows, static_cast<float*>(y.ptr), L0.n,
+                              EPI_STORE, nullptr, 0, mode, rtz, sc, stream->s);
+        };
+        round();  // warm-up (module load, shared-memory opt-in)
+        cudaEvent_t e0, e1;
+        BC_CUDA(cudaEventCreate(&e0));
+        BC_CUDA(cudaEventCreate(&e1));
+        BC_CUDA(cudaEventRecord(e0, stream->s));
+        for (int it = 0; it < iters; ++it) round();
+        BC_CUDA(cudaEventRecord(e1, stream->s));
+        BC_CUDA(cudaEventSynchronize(e1));
+        float ms = 0.0f;
+        BC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        check_stream_timeout(stream);
+        *out_avg_us = ms * 1000.0f / (float)(iters * n_w);
+        const int64_t wbytes = L0.n * (L0.k / block_size(L0.dtype)) * block_bytes(L0.dtype);
+        *out_bytes = (uint64_t)(wbytes + rows * L0.k * (x16 ? 2 : 4) + rows * L0.n * 4);
         return BEACON_CUDA_OK;
     });
 }

@@ -38,9 +38,10 @@ for _p in (REPO, os.path.join(REPO, "beacon-ai_b200")):
 
 WORKLOADS = {
     "llama3-8b-q4k": dict(shape="LLAMA3_8B", context=4096, batch=1,
-                          name="Llama-3-8B-shape decoder, Q4_K linears, f16 KV, batch 1, context 4096, greedy decode"),
+                          name="Llama-3-8B-shape decoder, Q4_K linears, f16 KV, batch {batch}, context 4096, "
+                               "greedy decode"),
     "llama3-70b-q4k-tp": dict(shape="LLAMA3_70B", context=8192, batch=1,
-                              name="Llama-3-70B-shape decoder, Q4_K linears, f16 KV, tensor-parallel, batch 1, "
+                              name="Llama-3-70B-shape decoder, Q4_K linears, f16 KV, tensor-parallel, batch {batch}, "
                                    "context 8192, greedy decode"),
     # prefill (time to first token); its own line, not the decode metric
     "llama3-8b-q8_0-prefill": dict(shape="LLAMA3_8B", context=2048, batch=4,
@@ -48,6 +49,17 @@ WORKLOADS = {
                                         "prompts (time to first token)"),
 }
 METRIC = "decode tok/s"
+# What the timed decode computes in (fast numerics).
+FAST_DTYPE = ("q4_k weights; activations quantised to int16 per 32-element block (fast numerics), integer dot "
+              "products; attention scores and P.V on f16 MMAs (query split into f16 high/low parts, P rounded to "
+              "f16); f32 accumulation and softmax")
+# The op-level dequant-GEMV sweep (weight shapes out x in, formats, batches).
+SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+SWEEP_BATCHES = (1, 4, 16)
+
+
+def workload_name(wl, batch, layers=0):
+    return WORKLOADS[wl]["name"].format(batch=batch) + (f" (REDUCED to {layers} layers)" if layers else "")
 
 
 def parse():
@@ -59,6 +71,8 @@ def parse():
     p.add_argument("--workload", choices=["auto"] + list(WORKLOADS), default="auto")
     p.add_argument("--batch", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-sweep", action="store_true", help="skip the op-level dequant-GEMV sweep")
+    p.add_argument("--no-exact", action="store_true", help="skip the exact-numerics decode figure")
     p.add_argument("--layers", type=int, default=0,
                    help="profiling only: build the workload with this many layers (the line says so)")
     p.add_argument("--profile-run", action="store_true",
@@ -153,7 +167,7 @@ class CpuDecodeSample:
     (full vocabulary, same context); one step times one decode token per
     sequence on both and extrapolates to full depth."""
 
-    def __init__(self, wl, batch):
+    def __init__(self, wl, batch, ref_faithful=False):
         import numpy as np
 
         import oracle as orc
@@ -175,7 +189,8 @@ class CpuDecodeSample:
         for nl in (1, 2):
             cfg = orc.OracleModelConfig(V, H, nl, shp["num_heads"], shp["num_kv_heads"], shp["head_dim"], F,
                                         self.ctx + 2, shp["rope_theta"], shp["rms_norm_eps"], kv_persist=True,
-                                        causal_prefill=True, weights_rtz=True)
+                                        causal_prefill=True, weights_rtz=True, threads=1 if ref_faithful else 0,
+                                        ref_faithful=ref_faithful)
             m = orc.OracleModel(cfg)
             m.set_weight(0, orc.W_EMBED, np.tile(emb_row, V), orc.F16)
             m.set_weight(0, orc.W_FINAL_NORM, np.ones(H, np.float16), orc.F16)
@@ -186,25 +201,28 @@ class CpuDecodeSample:
                 for w, (n, k) in ((orc.W_Q, (QD, H)), (orc.W_K, (KD, H)), (orc.W_V, (KD, H)), (orc.W_O, (H, QD)),
                                   (orc.W_GATE, (F, H)), (orc.W_UP, (F, H)), (orc.W_DOWN, (H, F))):
                     m.set_weight(li, w, rows(n, k), orc.Q4_K)
-            m.forward([1], self.ctx)  # warm the caches
+            if not ref_faithful:
+                m.forward([1], self.ctx)  # warm the caches
             self.models[nl] = m
 
     def step(self):
+        """(extrapolated tok/s, {layers: seconds}, seconds this sample took)."""
         t = {}
+        w0 = time.perf_counter()
         for nl, m in self.models.items():
             t0 = time.perf_counter()
             for b in range(self.batch):
                 m.forward([1 + b], self.ctx)  # one token per sequence at position `ctx`
             t[nl] = time.perf_counter() - t0
         t_tok = t[1] + (self.layers - 1) * max(t[2] - t[1], 0.0)
-        return self.batch / t_tok, t
+        return self.batch / t_tok, t, time.perf_counter() - w0
 
 
-def cpu_decode_sample(wl, batch, reps=3):
-    s = CpuDecodeSample(wl, batch)
+def cpu_decode_sample(wl, batch, reps=3, ref_faithful=False):
+    s = CpuDecodeSample(wl, batch, ref_faithful)
     best = None
     for _ in range(reps):
-        v, t = s.step()
+        v, t, _ = s.step()
         if best is None or v > best[0]:
             best = (v, t)
     return best
@@ -331,20 +349,23 @@ def run_ours(a):
     e2e_ms = max_over_ranks(max(f0.elapsed_time(f1), wall * 1e3))
     e2e_value = a.steps * batch / (e2e_ms / 1e3)
 
-    # --- roofline of the dominant kernel: fused gate/up GEMV over all layers ---
+    # --- roofline of the dominant kernel: fused gate/up projection over all layers ---
     us, nbytes = model.profile_linear(L.W_GATE, batch, 3)
     achieved = nbytes / (us * 1e-6) / 1e9
     peak, peak_kind = peaks()
     traffic = traffic_for(f"gate_up_{wl}_b{batch}")
-
+    kernel = ("qgemv3_kernel<Q4_K, FAST, B=%d> (persistent dequant-GEMV, fused gate/up + SwiGLU)" % batch
+              if batch <= 16 else
+              "qgemm_tc_kernel<Q4_K> (tcgen05 dequant-GEMM, fused gate/up + SwiGLU, M=%d)" % batch)
+    mem_gb = model.memory_bytes() / 1e9
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "q4_k weights, f32 accumulate",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": FAST_DTYPE,
         "data": "synthetic (seeded random weights; KV context filled with seeded random rows)",
-        "config": {"workload": WORKLOADS[wl]["name"] + (f" (REDUCED to {a.layers} layers)" if a.layers else ""),
+        "config": {"workload": workload_name(wl, batch, a.layers),
                    "model_shape": wl, "batch": batch, "context": ctx_len,
-                   "parallelism": f"tp{world}", "l2": f"inputs larger than L2: {model.memory_bytes() / 1e9:.1f} GB "
+                   "parallelism": f"tp{world}", "l2": f"inputs larger than L2: {mem_gb:.1f} GB "
                                                      "of weights and cache are read every step"},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 + 4 * batch,
@@ -352,25 +373,109 @@ def run_ours(a):
         "gpu_launches": launches * a.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "qgemv3_kernel<Q4_K, FAST, B=%d> (fused gate/up + SwiGLU), %.2f us/launch, "
-                               "%d algorithmic bytes/launch, peak %s" % (batch, us, nbytes, peak_kind)},
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel and "
+                                       "shape (profiles/traffic.txt); null when not captured",
+                     "kernel": "%s, %.2f us/launch (CUDA events, back-to-back over every layer's weights), "
+                               "%d algorithmic bytes/launch, peak %s" % (kernel, us, nbytes, peak_kind)},
     }
     if clk:
         out["clocks"] = clk
+    model.close()
+    del model
+    # the same decode in the exact numerics (f32 activations, f32 attention)
+    if world == 1 and not a.no_exact:
+        out["exact_numerics"] = exact_decode(a, shp, ctx_len, batch, max_ctx)
+    if world == 1 and not a.no_sweep:
+        out["gemv_sweep"] = gemv_sweep(be, peak)
+        out["gemv_sweep_note"] = ("quantized_matmul's decode path through beacon_cuda_profile_quantized_matmul, fp16 "
+                                  "activations, fast numerics, weights cycled over copies totalling >= 4x L2 (every "
+                                  "launch reads its weights from HBM); bytes = N*K*bpe + B*K*2 + B*N*4; frac of the "
+                                  "%s HBM peak" % peak_kind)
+    be.close()
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         tps, parts = cpu_decode_sample(wl, batch)
         out["cpu_baseline"] = {"value": round(tps, 4), "unit": "tok/s", "cores": host_threads(), "kind": "port",
-                               "sample": "oracle engine, 1- and 2-layer copies of the model (full vocab) decoding one "
-                                         "token at position %d; t1=%.3fs t2=%.3fs, extrapolated to %d layers"
+                               "sample": "oracle engine (row-parallel on all host cores, same sums as the reference), "
+                                         "1- and 2-layer copies of the model (full vocab) decoding one token at "
+                                         "position %d; t1=%.3fs t2=%.3fs, extrapolated to %d layers"
                                          % (ctx_len, parts[1], parts[2], shp["num_layers"])}
-    model.close()
-    del model
-    be.close()
+        tps1, parts1 = cpu_decode_sample(wl, batch, reps=1, ref_faithful=True)
+        out["cpu_baseline_ref_faithful"] = {
+            "value": round(tps1, 5), "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": "the reference's own loop order, one thread: per-call transposed copy of each weight "
+                      "(cpu_backend.rs:330-366) and the column-strided matmul_f32 (ops.rs:16-30); 1- and 2-layer "
+                      "copies of the model decoding one token at position %d; t1=%.2fs t2=%.2fs, extrapolated to "
+                      "%d layers" % (ctx_len, parts1[1], parts1[2], shp["num_layers"])}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def exact_decode(a, shp, ctx_len, batch, max_ctx):
+    """Device-resident greedy decode of the same workload in the exact numerics."""
+    import torch
+
+    from beacon_cuda import CudaBackend, CudaModel, DecoderConfig
+    from beacon_cuda import _lib as L
+    from beacon_cuda.synthetic import load_synthetic
+    be = CudaBackend(0, L.NUMERICS_EXACT)
+    model = CudaModel(be, DecoderConfig(**shp, max_context=max_ctx, max_batch=batch, numerics=L.NUMERICS_EXACT,
+                                        kv_dtype=L.DTYPE_F16))
+    load_synthetic(model, L.DTYPE_Q4_K, seed=0)
+    model.fill_kv_random(ctx_len, seed=1)
+    ts = torch.cuda.ExternalStream(model.stream.cuda_stream)
+    tok0 = torch.tensor([17 + b for b in range(batch)], dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    model.decode_step_device(tok0.data_ptr(), batch, ctx_len)
+    for _ in range(a.warmup - 1):
+        model.decode_step_device(None, batch, -1)
+    model.synchronize()
+    steps = min(a.steps, 64)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ts)
+    for _ in range(steps):
+        model.decode_step_device(None, batch, -1)
+    e1.record(ts)
+    e1.synchronize()
+    model.synchronize()
+    ms = e0.elapsed_time(e1)
+    model.close()
+    be.close()
+    return {"value": round(steps * batch / (ms / 1e3), 2), "unit": "tok/s", "steps": steps,
+            "ms_per_step": round(ms / steps, 4),
+            "dtype": "q4_k weights dequantised to their f32 values (q*d), f32 activations, f32 attention on the "
+                     "CUDA cores, f32 accumulation; f16 KV cache"}
+
+
+def gemv_sweep(be, peak):
+    """Op-level dequant-GEMV sweep: every shape x format x batch of the
+    configuration, through the op's decode path, L2-cold."""
+    import numpy as np
+    import torch
+
+    from beacon_cuda import _lib as L
+    from beacon_cuda.synthetic import quantize_on_device
+    s = be.new_stream()
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    rng = np.random.default_rng(0)
+    rows = []
+    for dt, name in ((L.DTYPE_Q4_0, "q4_0"), (L.DTYPE_Q8_0, "q8_0"), (L.DTYPE_Q4_K, "q4_k")):
+        for n, k in SWEEP_SHAPES:
+            raw = quantize_on_device(be, s, n, k, dt, seed=3, layer=n // 1024, slot=k // 1024)
+            copies = max(2, -(-4 * l2 // raw.numel()))
+            ws = [be.from_device_blocks(raw.data_ptr(), (n, k), dt) for _ in range(copies)]
+            del raw
+            x = rng.standard_normal((16, k)).astype(np.float16)
+            for b in SWEEP_BATCHES:
+                us, nb = be.profile_quantized_matmul(s, ws, be.upload(x[:b]), iters=max(3, 240 // copies))
+                gbs = nb / (us * 1e-6) / 1e9
+                rows.append({"format": name, "n": n, "k": k, "batch": b, "us": round(us, 3), "gb_s": round(gbs, 1),
+                             "frac": round(gbs / peak, 4)})
+            del ws
+            torch.cuda.empty_cache()
+    return rows
 
 
 def run_prefill(a):
@@ -424,7 +529,7 @@ def run_prefill(a):
            "warmup": min(a.warmup, 3), "ms_per_step": round(ttft_ms, 3), "ttft_ms": round(ttft_ms, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights, f16 MMA, f32 accumulate",
            "data": "synthetic (seeded random weights and prompt tokens)",
-           "config": {"workload": WORKLOADS[wl]["name"] + (f" (REDUCED to {a.layers} layers)" if a.layers else ""),
+           "config": {"workload": workload_name(wl, NB, a.layers),
                       "model_shape": wl, "batch": NB, "prompt": P, "parallelism": "tp1"},
            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                         "frac": round(tflops / peak, 4), "traffic": None,
@@ -437,29 +542,38 @@ def run_prefill(a):
 
 
 def run_reference(a):
+    """The reference's CPU path (the oracle port: the reference is Rust and no
+    Rust toolchain exists here) on the host cores, on rank 0 only. Each step is
+    one bounded sample: one decode token through 1- and 2-layer copies of the
+    model, extrapolated to full depth. ms_per_step is the wall time a sample
+    actually took; value is the extrapolated full-depth rate."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     wl = a.workload
     batch = a.batch or WORKLOADS[wl]["batch"]
     sample = CpuDecodeSample(wl, batch)
-    vals = []
+    vals, walls = [], []
     steps = min(a.steps, 32)  # each step is a bounded CPU sample; keep the run to a few minutes
     for i in range(a.warmup + steps):
-        tps, _ = sample.step()
+        tps, _, wall = sample.step()
         if i >= a.warmup:
             vals.append(tps)
+            walls.append(wall)
     v = statistics.mean(vals)
     shp = shape_of(wl)
     out = {"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": a.gpus, "steps": len(vals),
-           "warmup": a.warmup, "ms_per_step": round(1e3 * batch / v, 2), "higher_is_better": True,
+           "warmup": a.warmup, "ms_per_step": round(1e3 * statistics.mean(walls), 2), "higher_is_better": True,
+           "extrapolated_ms_per_token": round(1e3 * batch / v, 2),
            "scaling": "strong" if a.gpus > 1 else "weak", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic", "impl": "reference",
-           "config": {"workload": WORKLOADS[wl]["name"], "model_shape": wl, "batch": batch,
+           "config": {"workload": workload_name(wl, batch), "model_shape": wl, "batch": batch,
                       "context": WORKLOADS[wl]["context"], "parallelism": "host cores"},
            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": host_threads(), "kind": "port",
-                            "sample": "CPU restatement of the reference engine (oracle/), 1- and 2-layer copies of "
-                                      "the model at the full context, extrapolated to %d layers" % shp["num_layers"]},
+                            "sample": "CPU restatement of the reference engine (oracle/, row-parallel on all host "
+                                      "cores, the reference's sums and their order), one decode token through 1- and "
+                                      "2-layer copies of the model at the full context, extrapolated to %d layers"
+                                      % shp["num_layers"]},
            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 

@@ -100,6 +100,17 @@ typedef enum {
 int32_t beacon_cuda_context_create(int32_t device, BeaconCudaContext** out_ctx);
 void    beacon_cuda_context_destroy(BeaconCudaContext* ctx);
 int32_t beacon_cuda_context_set_numerics(BeaconCudaContext* ctx, int32_t numerics);
+/* Limit, in SM clock cycles, of every bounded device-side wait on progress
+ * (tile copies, pipeline stages, split merges) of the kernels on this
+ * context's device; 0 restores the default 2^31 (about 1.1 s at 1965 MHz).
+ * A wait that runs out makes its kernel record the failure, let the work it
+ * already issued finish, and return. The failure is reported as
+ * BEACON_CUDA_ERR_DEVICE_TIMEOUT by the next synchronising call
+ * (stream_synchronize, tensor_eval, tensor_read_*, model_decode_step,
+ * model_forward, model_synchronize), which also resets the scratch counters
+ * so the context stays usable. No reference counterpart (the reference runs
+ * no device code); shim/src/guard.h:12-39 is the status convention. */
+int32_t beacon_cuda_context_set_wait_limit(BeaconCudaContext* ctx, int64_t cycles);
 
 int32_t beacon_cuda_stream_create(BeaconCudaContext* ctx, BeaconCudaStream** out_stream);
 /* Borrow an existing cudaStream_t (passed as void*); destroy does not free it. */
@@ -202,6 +213,18 @@ int32_t beacon_cuda_create_token_tensor(BeaconCudaContext* ctx, const uint32_t* 
  * among equal maxima, NaN compares equal (sampling.rs:60-66). out: I32 [rows]. */
 int32_t beacon_cuda_op_argmax(BeaconCudaContext* ctx, BeaconCudaStream* stream,
                               const BeaconCudaTensor* logits, BeaconCudaTensor** out);
+/* Measurement of quantized_matmul's decode path (rows 1..16): times `iters`
+ * rounds of the op's own plan, kernels and scratch over the weights
+ * w[0..n_w) in turn (same block type and shape; distinct copies whose total
+ * exceeds L2 make every launch read its weights from HBM), with CUDA events
+ * on `stream`. out_avg_us: mean duration of one launch; out_bytes:
+ * algorithmic bytes of one launch (weight blocks + activations + f32 out).
+ * No reference counterpart: the reference's kernel benches
+ * (crates/beacon-kernels/benches/kernels.rs:88-108) time q4_matmul_f32. */
+int32_t beacon_cuda_profile_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                                             const BeaconCudaTensor* const* w, int32_t n_w,
+                                             const BeaconCudaTensor* x, int32_t iters, float* out_avg_us,
+                                             uint64_t* out_bytes);
 /* dequantize_to_f16 (dequant.rs:33-60), bit-exact: out F16 [N, K]. */
 int32_t beacon_cuda_op_dequantize_to_f16(BeaconCudaContext* ctx, BeaconCudaStream* stream,
                                          const BeaconCudaTensor* w, BeaconCudaTensor** out);
@@ -279,11 +302,17 @@ int32_t beacon_cuda_model_decode_step(BeaconCudaModel* model, BeaconCudaStream* 
                                       const uint32_t* tokens, int32_t batch, int32_t position,
                                       uint32_t* next_tokens, float* logits_out);
 /* Same step with device buffers (int32 tokens in, int32 next tokens out,
- * logits F32 [batch, vocab] or NULL); enqueued only, nothing is copied. */
+ * logits F32 [batch, vocab] or NULL); enqueued only, nothing is copied.
+ * Device-side errors of enqueued steps (context overflow, bounded waits that
+ * ran out) are reported by the next model_synchronize / decode_step / forward. */
 int32_t beacon_cuda_model_decode_step_device(BeaconCudaModel* model, BeaconCudaStream* stream,
                                              const int32_t* d_tokens, int32_t batch,
                                              int32_t position, int32_t* d_next_tokens,
                                              float* d_logits);
+/* Waits for the model's work on `stream` and reports its device-side errors:
+ * CONTEXT_OVERFLOW, SHAPE_MISMATCH (token id out of range) or DEVICE_TIMEOUT.
+ * (Engine::generate_next_token's error paths, engine.rs:249-264.) */
+int32_t beacon_cuda_model_synchronize(BeaconCudaModel* model, BeaconCudaStream* stream);
 /* Times `iters` passes of one projection over every layer, using the model's
  * own kernels and buffers (each layer's weight is distinct, so reads are
  * L2-cold), with CUDA events on `stream`. slot: BEACON_CUDA_W_Q (the fused

@@ -313,7 +313,8 @@ class _Cfg(ctypes.Structure):
         "intermediate_size", "max_context")] + [
         ("rope_theta", ctypes.c_float), ("rms_norm_eps", ctypes.c_float),
         ("kv_persist", ctypes.c_int32), ("causal_prefill", ctypes.c_int32),
-        ("weights_rtz", ctypes.c_int32), ("threads", ctypes.c_int32)]
+        ("weights_rtz", ctypes.c_int32), ("threads", ctypes.c_int32),
+        ("ref_faithful", ctypes.c_int32)]
 
 
 @dataclass
@@ -332,6 +333,7 @@ class OracleModelConfig:
     causal_prefill: bool = True
     weights_rtz: bool = True
     threads: int = 0
+    ref_faithful: bool = False   # the reference's transpose + column-strided matmul, one thread
 
 
 class OracleModel:
@@ -342,7 +344,7 @@ class OracleModel:
         c = _Cfg(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
                  cfg.num_kv_heads, cfg.head_dim, cfg.intermediate_size, cfg.max_context,
                  cfg.rope_theta, cfg.rms_norm_eps, int(cfg.kv_persist),
-                 int(cfg.causal_prefill), int(cfg.weights_rtz), cfg.threads)
+                 int(cfg.causal_prefill), int(cfg.weights_rtz), cfg.threads, int(cfg.ref_faithful))
         self._h = lib().orc_model_create(ctypes.byref(c))
         if not self._h:
             raise RuntimeError("orc_model_create failed")

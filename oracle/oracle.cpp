@@ -769,6 +769,15 @@ struct Model {
 // transpose only relabels W, so reading W row-major gives the same sums.
 void linear(const Model& m, const float* x, size_t rows, const std::vector<float>& w,
             size_t n, size_t k, float* y) {
+    if (m.cfg.ref_faithful) {
+        // the reference's own loop order, single-threaded: transpose W [n, k]
+        // into a new [k, n] buffer on every call, then matmul_f32 with its
+        // column-strided inner loop
+        std::vector<float> wt(n * k);
+        orc_transpose_f32(w.data(), wt.data(), 1, n, k);
+        orc_matmul_f32(x, wt.data(), y, rows, k, n);
+        return;
+    }
     int threads = m.cfg.threads;
 #ifdef _OPENMP
     if (threads <= 0) threads = omp_get_max_threads();

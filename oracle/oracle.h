@@ -91,6 +91,11 @@ typedef struct {
     int32_t weights_rtz;     /* 1 = weights f16_to_f32(dequantize_to_f16(.)) as the
                                 CPU engine consumes them; 0 = unrounded q*d */
     int32_t threads;
+    int32_t ref_faithful;    /* 1 = every projection runs as the reference does it:
+                                a fresh transposed copy of W per call
+                                (cpu_backend.rs:330-366) then the column-strided
+                                matmul_f32 loop (ops.rs:16-30), one thread. Same
+                                sums in the same order, so the same results. */
 } OrcModelConfig;
 
 enum {

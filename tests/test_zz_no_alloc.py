@@ -48,6 +48,7 @@ def test_noalloc_matches_quantized_matmul_on_two_calls(be, dtype, n, k, batch, x
     xt = be.upload(x)
     s = be.new_stream()
     ref = be.quantized_matmul(s, xt, wt).numpy()
+    orc_ref = orc.qgemv(w, dtype, n, k, x.astype(np.float32))
     yt = be.zeros((batch, n))
     for call in range(2):
         st = L.lib().beacon_cuda_quantized_matvec_noalloc(
@@ -57,6 +58,73 @@ def test_noalloc_matches_quantized_matmul_on_two_calls(be, dtype, n, k, batch, x
         s.synchronize()
         got = yt.numpy()
         assert _rel(got, ref) <= GEMV_TOL, (call, _rel(got, ref))
+        assert _rel(got, orc_ref) <= GEMV_TOL, (call, _rel(got, orc_ref))
+
+
+def test_noalloc_allocates_nothing_under_graph_capture(be):
+    """After a first call on the device, a call captured into a CUDA graph in
+    the global capture mode (which makes any cudaMalloc fail the capture)
+    replays correctly, and the device's free memory is unchanged."""
+    import torch
+    from beacon_cuda import _lib as L
+    rng = np.random.default_rng(7)
+    n, k, batch = 4096, 4096, 1
+    w = orc.quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32), orc.Q4_K)
+    wt = be.upload(w, shape=(n, k), dtype=orc.Q4_K)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    xt, yt = be.upload(x), be.zeros((batch, n))
+    ts = torch.cuda.Stream()
+    import ctypes as C
+    sh = C.c_void_p()
+    L.check(L.lib().beacon_cuda_stream_wrap(be.ctx, C.c_void_p(ts.cuda_stream), C.byref(sh)))
+    try:
+        def call():
+            L.check(L.lib().beacon_cuda_quantized_matvec_noalloc(sh, wt.handle, C.c_void_p(xt.device_ptr),
+                                                                 L.DTYPE_F32, batch, C.c_void_p(yt.device_ptr)))
+        call()  # first call on the device: looks the scratch array up
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=ts):
+            call()
+        free1 = torch.cuda.mem_get_info()[0]
+
+        class _View:  # the output buffer seen by torch without a copy
+            __cuda_array_interface__ = {"shape": (batch, n), "typestr": "<f4", "data": (yt.device_ptr, False),
+                                        "version": 3}
+        y_view = torch.as_tensor(_View(), device="cuda")
+        for _ in range(2):
+            y_view.fill_(float("nan"))  # the replay alone must produce the result
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            got = yt.numpy()
+            assert _rel(got, orc.qgemv(w, orc.Q4_K, n, k, x)) <= GEMV_TOL
+        free2 = torch.cuda.mem_get_info()[0]
+        # the graph itself may hold a little driver memory; the call none
+        assert free0 - free1 <= 4 << 20 and free1 == free2, (free0, free1, free2)
+        del g
+    finally:
+        L.lib().beacon_cuda_stream_destroy(sh)
+
+
+def test_noalloc_rejects_a_stream_of_another_context(be):
+    from beacon_cuda import CudaBackend
+    from beacon_cuda import _lib as L
+    rng = np.random.default_rng(8)
+    w = orc.quantize((rng.standard_normal((64, 256)) * 0.02).astype(np.float32), orc.Q4_K)
+    wt = be.upload(w, shape=(64, 256), dtype=orc.Q4_K)
+    xt, yt = be.zeros((1, 256)), be.zeros((1, 64))
+    other = CudaBackend(0)
+    try:
+        s2 = other.new_stream()
+        st = L.lib().beacon_cuda_quantized_matvec_noalloc(s2.handle, wt.handle, ctypes.c_void_p(xt.device_ptr),
+                                                          L.DTYPE_F32, 1, ctypes.c_void_p(yt.device_ptr))
+        assert st == L.ERR_INVALID_ARGUMENT
+        assert b"another context" in L.lib().beacon_cuda_last_error_message()
+        del s2
+    finally:
+        other.close()
 
 
 def test_noalloc_rejects_bad_arguments(be):
