@@ -199,12 +199,30 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* ptr, int v) {
     return old;
 }
 
-// Bounded wait on progress; false if the runtime limit was reached.
+// Non-blocking test of a phase (no suspension).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on progress; false if the runtime limit was reached. At the
+// default limit the wait uses try_wait, which lets the hardware suspend the
+// thread; a shortened limit polls with test_wait so that the limit, not the
+// hardware's suspend interval, decides when the wait gives up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long limit = *(volatile long long*)&g_wait_limit;
+    const long long limit = g_wait_limit;  // constant during a kernel
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity))
+    if (limit >= kBoundedWaitLimit) {
+        while (!mbar_try_wait(bar, parity))
+            if (clock64() - t0 > limit) return false;
+        return true;
+    }
+    while (!mbar_test_wait(bar, parity))
         if (clock64() - t0 > limit) return false;
     return true;
 }

@@ -27,6 +27,7 @@
 #pragma once
 
 #include "gemv.cuh"
+#include "gemv_mma.cuh"
 
 namespace bc {
 
@@ -442,8 +443,9 @@ __device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, u
     if (lane == 0) a.counters[g] = 0;
 }
 
-template <int FMT, int MODE, int B>
+template <int FMT, int MODE, int B, bool MMA>
 __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel(const Gemv3Params a, const int epi) {
+    static_assert(!MMA || MODE == MODE_FAST, "the tensor-core consumer serves the fast numerics");
     extern __shared__ __align__(128) uint8_t g3_smem[];
     uint8_t* smem = g3_smem;
     const GemvParams& p = a.p;
@@ -547,26 +549,51 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     uint32_t g = rg.wb / KT;      // row group of the current tile
     uint32_t t = rg.wb - g * KT;  // its k-tile
     int i = 0;
+    // tensor-core consumer: per-warp scratch after the split-K partials
+    float* scr = red + kG3Warps * 2 * B * 32 + warp * mma_scratch_floats<FMT, B>();
+    MmaAcc macc;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) macc.v[r][0] = macc.v[r][1] = 0.0f;
     for (; i < n; ++i) {
         const int st = i % S;
         if (!mbar_wait_bounded(&mybar[st], (uint32_t)((i / S) & 1))) {
             ok = false;
             break;
         }
-        G3Tile<FMT> tile;
-        g3_load_tile<FMT>(myring + (size_t)st * tb, lane, tile);
-        __syncwarp();
-        if (lane == 0 && i + S < n) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_expect_tx(&mybar[st], (uint32_t)tb);
-            bulk_g2s(myring + (size_t)st * tb, p.w + (t_begin + i + S) * tb, (uint32_t)tb, &mybar[st]);
+        const uint8_t* tp = myring + (size_t)st * tb;
+        auto refill = [&]() {
+            if (lane == 0 && i + S < n) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_expect_tx(&mybar[st], (uint32_t)tb);
+                bulk_g2s(myring + (size_t)st * tb, p.w + (t_begin + i + S) * tb, (uint32_t)tb, &mybar[st]);
+            }
+        };
+        if constexpr (MMA) {
+            MmaTileRegs<FMT> regs;
+            mma_load_tile<FMT>(tp, lane, regs);
+            mma_scales<FMT>(tp, lane, scr);
+            __syncwarp();
+            if (FMT != FMT_Q8_0) refill();  // Q4 tiles are in registers now
+            mma_consume_tile<FMT, B>(regs, tp, xs, a.kspan, (int)t, scr, macc, lane);
+            if (FMT == FMT_Q8_0) {
+                __syncwarp();
+                refill();
+            }
+        } else {
+            G3Tile<FMT> tile;
+            g3_load_tile<FMT>(tp, lane, tile);
+            __syncwarp();
+            refill();
+            g3_consume_tile<FMT, MODE, B>(tile, xs, a.kspan, (int)t, acc, rtz);
         }
-        g3_consume_tile<FMT, MODE, B>(tile, xs, a.kspan, (int)t, acc, rtz);
         // end of a row group (or of this warp's range): finish it
         if (t == KT - 1 || i == n - 1) {
+            if constexpr (MMA) mma_rows_to_lanes<B>(macc, scr, acc, lane);
             g3_finish_group<B>(a, epi, g, KT, lane, acc, inv, red, cta_cnt, pre);
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = 0.0f;
+        } else if constexpr (MMA) {
+            __syncwarp();  // the tile's scales have been read before the next tile's overwrite them
         }
         if (++t == KT) {
             t = 0;
@@ -584,8 +611,13 @@ inline size_t gemv3_x_bytes(int mode, int bpad, int64_t kspan) {
     return mode == MODE_F32 ? (size_t)bpad * kspan * 4 : (size_t)bpad * kspan * 2 + (size_t)bpad * (kspan / 32) * 8;
 }
 inline size_t gemv3_bar_bytes(int stages) { return 128 * (((size_t)kG3Warps * stages * 8 + 127) / 128); }
+// Per-CTA scratch of the tensor-core consumer (block scales / row transpose).
+inline size_t gemv3_mma_bytes(int32_t dtype, int bpad) {
+    const size_t scales = dtype == BEACON_CUDA_DTYPE_Q4_K ? 512 : 256;
+    return (size_t)kG3Warps * 4 * std::max<size_t>(scales, (size_t)32 * bpad);
+}
 
-template <int FMT, int MODE, int B>
+template <int FMT, int MODE, int B, bool MMA>
 void launch_qgemv3_t(const LinearPlan& pl, const GemvLaunch& a) {
     Gemv3Params q;
     GemvParams& p = q.p;
@@ -621,26 +653,34 @@ void launch_qgemv3_t(const LinearPlan& pl, const GemvLaunch& a) {
     q.slots = a.scratch.partial;
     q.counters = a.scratch.counters;
     q.err = a.scratch.err;
-    auto kern = qgemv3_kernel<FMT, MODE, B>;
+    auto kern = qgemv3_kernel<FMT, MODE, B, MMA>;
     allow_max_dynamic_smem(kern);
     launch_kernel(kern, dim3((unsigned)pl.nctas), dim3(kG3Warps * 32), pl.smem, a.s, a.pdl, q, a.epi);
 }
 
 template <int FMT>
 void launch_qgemv3_fmt(const LinearPlan& pl, const GemvLaunch& a) {
+    if (a.mode == MODE_FAST && pl.mma) {
+        switch (pl.bpad) {
+            case 1: return launch_qgemv3_t<FMT, MODE_FAST, 1, true>(pl, a);
+            case 2: return launch_qgemv3_t<FMT, MODE_FAST, 2, true>(pl, a);
+            case 4: return launch_qgemv3_t<FMT, MODE_FAST, 4, true>(pl, a);
+            default: return launch_qgemv3_t<FMT, MODE_FAST, 8, true>(pl, a);
+        }
+    }
     if (a.mode == MODE_FAST) {
         switch (pl.bpad) {
-            case 1: return launch_qgemv3_t<FMT, MODE_FAST, 1>(pl, a);
-            case 2: return launch_qgemv3_t<FMT, MODE_FAST, 2>(pl, a);
-            case 4: return launch_qgemv3_t<FMT, MODE_FAST, 4>(pl, a);
-            default: return launch_qgemv3_t<FMT, MODE_FAST, 8>(pl, a);
+            case 1: return launch_qgemv3_t<FMT, MODE_FAST, 1, false>(pl, a);
+            case 2: return launch_qgemv3_t<FMT, MODE_FAST, 2, false>(pl, a);
+            case 4: return launch_qgemv3_t<FMT, MODE_FAST, 4, false>(pl, a);
+            default: return launch_qgemv3_t<FMT, MODE_FAST, 8, false>(pl, a);
         }
     }
     switch (pl.bpad) {
-        case 1: return launch_qgemv3_t<FMT, MODE_F32, 1>(pl, a);
-        case 2: return launch_qgemv3_t<FMT, MODE_F32, 2>(pl, a);
-        case 4: return launch_qgemv3_t<FMT, MODE_F32, 4>(pl, a);
-        default: return launch_qgemv3_t<FMT, MODE_F32, 8>(pl, a);
+        case 1: return launch_qgemv3_t<FMT, MODE_F32, 1, false>(pl, a);
+        case 2: return launch_qgemv3_t<FMT, MODE_F32, 2, false>(pl, a);
+        case 4: return launch_qgemv3_t<FMT, MODE_F32, 4, false>(pl, a);
+        default: return launch_qgemv3_t<FMT, MODE_F32, 8, false>(pl, a);
     }
 }
 

@@ -77,7 +77,19 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     if (batch > 8) return pl;
     pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : 8;
     const size_t budget = 220 * 1024, half_sm = 110 * 1024;
-    const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad);
+    // The fast numerics consume tiles with the tensor-core (mma.sync) consumer
+    // from 4 rows on, and for Q8_0 (no nibble unpacking); 4-bit weights at 1-2
+    // rows keep the dp2a consumer, measured faster there (its per-row
+    // accumulation needs no transpose and no scale table).
+    // BEACON_CUDA_GEMV_MMA=0: dp2a everywhere; =2: tensor cores everywhere.
+    static const int mma_env = [] {
+        const char* e = std::getenv("BEACON_CUDA_GEMV_MMA");
+        return e ? std::atoi(e) : 1;
+    }();
+    const bool mma = mode == MODE_FAST && mma_env != 0 &&
+                     (mma_env == 2 || pl.bpad >= 4 || L.dtype == BEACON_CUDA_DTYPE_Q8_0);
+    const size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad) +
+                      (mma ? gemv3_mma_bytes(L.dtype, pl.bpad) : 0);
     const size_t tb = (size_t)L.tile_bytes;
     if (xb + 256 + 2 * kG3Warps * tb > budget) return pl;
     int stages = (int)std::min<size_t>(6, (budget - xb - 256) / (kG3Warps * tb));
@@ -109,6 +121,7 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     const int64_t per_cta = (total_tiles + nctas - 1) / nctas;
     if (per_cta / L.ktiles() + 2 > kG3MaxCtaGroups) return pl;  // the CTA's arrival counters
     pl.v3 = true;
+    pl.mma = mma;
     pl.stages = stages;
     pl.nctas = (int)nctas;
     pl.total_warps = nctas * kG3Warps;
@@ -118,6 +131,20 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     // leaving SMs idle), while one CTA of the next kernel still fits beside
     if (nctas <= sms && pairable) pl.smem = std::max<size_t>(pl.smem, kSpreadSmem);
     return pl;
+}
+
+// Rows of the next launch out of `rem` (1..16): the persistent kernel takes
+// up to 8 rows at a time; 9..16 rows go in 8-row launches (each reads the
+// weights again, still far faster than one 16-row launch of the tiled
+// kernel), and rows whose persistent plan does not fit shared memory (staged
+// activations of a long K) go in 4-, 2- or 1-row launches. When no persistent
+// plan fits at all, the tiled kernel takes them all.
+int linear_chunk_rows(const BeaconCudaContext* ctx, const QLayout& L, int rem, int mode) {
+    const int b = std::min(16, rem);
+    if (b <= 8 && plan_linear(ctx, L, b, mode).v3) return b;
+    for (int c : {8, 4, 2, 1})
+        if (c < b && plan_linear(ctx, L, c, mode).v3) return c;
+    return b;
 }
 
 size_t LinearPlan::scratch_floats(int batch, const QLayout& L) const {
@@ -211,8 +238,8 @@ void dense_qmatmul(BeaconCudaContext* ctx, BeaconCudaStream* stream, const Beaco
                         stream->ws.flags() + Workspace::kTimeoutFlag, s, x16);
         return;
     }
-    for (int64_t r0 = 0; r0 < rows; r0 += 16) {
-        const int b = (int)std::min<int64_t>(16, rows - r0);
+    for (int64_t r0 = 0, b = 0; r0 < rows; r0 += b) {
+        b = linear_chunk_rows(ctx, L, (int)std::min<int64_t>(rows - r0, 16), mode);
         LinearPlan pl = plan_linear(ctx, L, b, mode);
         GemvScratch sc = stream_gemv_scratch(stream, pl, b, L);
         launch_linear(pl, L, w->data(), static_cast<const uint8_t*>(x) + (size_t)r0 * L.k * eb, x_f16, L.k, b,

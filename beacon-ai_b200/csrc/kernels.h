@@ -143,6 +143,7 @@ void launch_qgemv_q4_k(const GemvLaunch& a);
 // staged activations fit in shared memory; otherwise the tiled GEMV above.
 struct LinearPlan {
     bool v3 = false;
+    bool mma = false;  // persistent kernel, fast numerics: tensor-core tile consumer
     GemvPlan v2;
     int nctas = 0, stages = 0, bpad = 1;
     size_t smem = 0;
@@ -150,6 +151,8 @@ struct LinearPlan {
     size_t scratch_floats(int batch, const QLayout& L) const;
 };
 LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode);
+// Rows (of up to 16 remaining) for the next GEMV launch.
+int linear_chunk_rows(const BeaconCudaContext* ctx, const QLayout& L, int rem, int mode);
 // norm_w (persistent plan only): y = W rmsnorm(x, norm_w, norm_eps).
 void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
                    int batch, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, int mode, bool rtz,

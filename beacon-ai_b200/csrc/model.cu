@@ -243,11 +243,7 @@ QxImage qx_image(BeaconCudaModel* m, int which, const QLayout& consumer, int row
 // that take the persistent kernel -- each reads the weights again, still far
 // faster than the tiled kernel -- else the tiled kernel takes them all.
 int gemv_rows(const BeaconCudaModel* m, const QLayout& L, int rem) {
-    const int b = std::min(16, rem);
-    if (b > 8 || plan_linear(m->ctx, L, b, gemv_mode(m)).v3) return b;
-    for (int c : {4, 2, 1})
-        if (c < b && plan_linear(m->ctx, L, c, gemv_mode(m)).v3) return c;
-    return b;
+    return linear_chunk_rows(m->ctx, L, rem, gemv_mode(m));
 }
 
 // qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.

@@ -572,12 +572,19 @@ int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream
             if (rows > 16) {
                 dense_qmatmul(ctx, stream, w, x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, rows,
                               static_cast<float*>(o->data()), ctx->numerics);
-            } else if (rows > 0) {
-                LinearPlan pl = plan_linear(ctx, w->q, (int)rows, mode);
-                GemvScratch sc = stream_gemv_scratch(stream, pl, (int)rows, w->q);
-                launch_linear(pl, w->q, w->data(), x->data(), x->dtype == BEACON_CUDA_DTYPE_F16, K, (int)rows,
-                              static_cast<float*>(o->data()), w->q.n, EPI_STORE, nullptr, 0, mode, rtz, sc,
-                              stream->s);
+            } else {
+                const bool x16 = x->dtype == BEACON_CUDA_DTYPE_F16;
+                for (int r0 = 0, b = 0; r0 < (int)rows; r0 += b) {
+                    b = linear_chunk_rows(ctx, w->q, (int)rows - r0, mode);
+                    LinearPlan pl = plan_linear(ctx, w->q, b, mode);
+                    GemvScratch sc = stream_gemv_scratch(stream, pl, b, w->q);
+                    // programmatic dependent launch: the weight stream may start
+                    // while the stream's previous kernel finishes (weights are
+                    // never written by other work; x is read after the wait)
+                    launch_linear(pl, w->q, w->data(), static_cast<const uint8_t*>(x->data()) + (size_t)r0 * K * (x16 ? 2 : 4),
+                                  x16, K, b, static_cast<float*>(o->data()) + (size_t)r0 * w->q.n, w->q.n, EPI_STORE,
+                                  nullptr, 0, mode, rtz, sc, stream->s, nullptr, 0.0f, /*pdl=*/true);
+                }
             }
         } catch (...) {
             delete o;
@@ -612,12 +619,20 @@ int32_t beacon_cuda_profile_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaS
         const bool rtz = ctx->numerics == BEACON_CUDA_NUMERICS_REF_RTZ;
         const bool x16 = x->dtype == BEACON_CUDA_DTYPE_F16;
         DeviceBuffer y((size_t)rows * L0.n * 4);
-        LinearPlan pl = plan_linear(ctx, L0, (int)rows, mode);
-        GemvScratch sc = stream_gemv_scratch(stream, pl, (int)rows, L0);
+        // the same row chunks as quantized_matmul
+        std::vector<int> chunks;
+        for (int r0 = 0, b = 0; r0 < (int)rows; r0 += b) chunks.push_back(b = linear_chunk_rows(ctx, L0, (int)rows - r0, mode));
+        std::vector<LinearPlan> plans;
+        std::vector<GemvScratch> scs;
+        for (int b : chunks) plans.push_back(plan_linear(ctx, L0, b, mode));
+        for (size_t c = 0; c < chunks.size(); ++c) scs.push_back(stream_gemv_scratch(stream, plans[c], chunks[c], L0));
         auto round = [&]() {
             for (int i = 0; i < n_w; ++i)
-                launch_linear(pl, L0, w[i]->data(), x->data(), x16, L0.k, (int)rows, static_cast<float*>(y.ptr), L0.n,
-                              EPI_STORE, nullptr, 0, mode, rtz, sc, stream->s);
+                for (size_t c = 0, r0 = 0; c < chunks.size(); r0 += chunks[c], ++c)
+                    launch_linear(plans[c], L0, w[i]->data(),
+                                  static_cast<const uint8_t*>(x->data()) + r0 * L0.k * (x16 ? 2 : 4), x16, L0.k,
+                                  chunks[c], static_cast<float*>(y.ptr) + r0 * L0.n, L0.n, EPI_STORE, nullptr, 0, mode,
+                                  rtz, scs[c], stream->s, nullptr, 0.0f, /*pdl=*/true);
         };
         round();  // warm-up (module load, shared-memory opt-in)
         cudaEvent_t e0, e1;
