@@ -37,6 +37,20 @@ W_EMBED, W_FINAL_NORM, W_LM_HEAD = 0, 1, 2
 W_ATTN_NORM, W_Q, W_K, W_V, W_O, W_FFN_NORM, W_GATE, W_UP, W_DOWN = 10, 11, 12, 13, 14, 15, 16, 17, 18
 
 
+class SamplingParams(ctypes.Structure):
+    """BeaconCudaSamplingParams: GenerationParams' sampling fields (params.rs:6-31)."""
+    _fields_ = [("temperature", ctypes.c_float), ("has_top_k", ctypes.c_int32), ("top_k", ctypes.c_int32),
+                ("has_top_p", ctypes.c_int32), ("top_p", ctypes.c_float), ("has_min_p", ctypes.c_int32),
+                ("min_p", ctypes.c_float), ("repeat_penalty", ctypes.c_float)]
+
+
+def sampling_params(temperature=0.0, top_k=None, top_p=None, min_p=None, repeat_penalty=1.0) -> SamplingParams:
+    """None means the Option field is None."""
+    return SamplingParams(temperature, top_k is not None, top_k or 0, top_p is not None,
+                          0.0 if top_p is None else top_p, min_p is not None, 0.0 if min_p is None else min_p,
+                          repeat_penalty)
+
+
 class BeaconCudaError(RuntimeError):
     """A non-OK status from the C ABI, with beacon_cuda_last_error_message()."""
 
@@ -98,6 +112,7 @@ SIGNATURES = {
     "beacon_cuda_op_argmax": (_I32, [_P, _P, _P, _PP]),
     "beacon_cuda_profile_quantized_matmul": (_I32, [_P, _P, _PP, _I32, _P, _I32, ctypes.POINTER(ctypes.c_float),
                                                     ctypes.POINTER(ctypes.c_uint64)]),
+    "beacon_cuda_op_sample": (_I32, [_P, _P, _P, _P, _P, _P, _PP]),
     "beacon_cuda_op_dequantize_to_f16": (_I32, [_P, _P, _P, _PP]),
     "beacon_cuda_op_quantize": (_I32, [_P, _P, _P, _I32, _I32, _PP]),
     "beacon_cuda_quantize_blocks": (_I32, [_P, _P, _P, _I64, _I64, _I32, _I32, _P]),
@@ -108,6 +123,7 @@ SIGNATURES = {
     "beacon_cuda_model_reset": (_I32, [_P]),
     "beacon_cuda_model_forward": (_I32, [_P, _P, _P, _I32, _I32, _P]),
     "beacon_cuda_model_decode_step": (_I32, [_P, _P, _P, _I32, _I32, _P, _P]),
+    "beacon_cuda_model_decode_step_sampled": (_I32, [_P, _P, _P, _I32, _I32, _P, _P, _P, _I32, _P]),
     "beacon_cuda_model_decode_step_device": (_I32, [_P, _P, _P, _I32, _I32, _P, _P]),
     "beacon_cuda_model_synchronize": (_I32, [_P, _P]),
     "beacon_cuda_model_profile_linear": (_I32, [_P, _P, _I32, _I32, _I32, ctypes.POINTER(ctypes.c_float),

@@ -288,6 +288,12 @@ class CudaBackend:
                                                             iters, ctypes.byref(us), ctypes.byref(nb)))
         return us.value, nb.value
 
+    def sample(self, stream: Stream, logits: Tensor, params: L.SamplingParams, uniforms: Tensor,
+               previous: Tensor | None = None) -> Tensor:
+        """sampling::sample (sampling.rs:15-57) per row on the device; I32 [rows]."""
+        return self._op(L.lib().beacon_cuda_op_sample, stream.handle, logits.handle,
+                        previous.handle if previous else None, ctypes.byref(params), uniforms.handle)
+
     def dequantize_to_f16(self, stream: Stream, w: Tensor) -> Tensor:
         return self._op(L.lib().beacon_cuda_op_dequantize_to_f16, stream.handle, w.handle)
 

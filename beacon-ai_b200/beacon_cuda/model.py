@@ -84,6 +84,20 @@ class CudaModel:
                                                      logits.ctypes.data if logits is not None else None))
         return nxt, logits
 
+    def decode_step_sampled(self, tokens, position: int, params: L.SamplingParams, uniforms,
+                            previous=None) -> np.ndarray:
+        """One step with the next tokens sampled on the device (no logits to the host).
+        uniforms: [batch] draws in [0, 1); previous: [batch, n] generated tokens or None."""
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        u = np.ascontiguousarray(np.asarray(uniforms, dtype=np.float32))
+        prev = None if previous is None else np.ascontiguousarray(np.asarray(previous, dtype=np.uint32))
+        n_prev = 0 if prev is None else prev.shape[-1]
+        nxt = np.empty(toks.size, dtype=np.uint32)
+        _raise(L.lib().beacon_cuda_model_decode_step_sampled(
+            self._h, self.stream.handle, toks.ctypes.data, toks.size, position, ctypes.byref(params), u.ctypes.data,
+            prev.ctypes.data if n_prev else None, n_prev, nxt.ctypes.data))
+        return nxt
+
     def decode_step_device(self, d_tokens: int | None, batch: int, position: int,
                            d_next: int | None = None, d_logits: int | None = None,
                            stream: Stream | None = None) -> None:

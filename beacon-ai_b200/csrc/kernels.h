@@ -179,6 +179,14 @@ GemvScratch stream_gemv_scratch(BeaconCudaStream* stream, const LinearPlan& pl, 
 void dense_qmatmul(BeaconCudaContext* ctx, BeaconCudaStream* stream, const BeaconCudaTensor* w, const void* x,
                    bool x_f16, int64_t rows, float* out, int numerics);
 
+// Token sampling (sample.cu): rows of logits [rows][ld] (V used) -> out[rows].
+struct ArgmaxSummary;
+void launch_sample(const float* logits, int64_t ld, int64_t V, int rows, const int32_t* prev, int n_prev,
+                   const BeaconCudaSamplingParams& p, const float* uniforms, float* work, int32_t* out,
+                   ArgmaxSummary* argmax_scratch, cudaStream_t s);
+// Scratch of launch_sample: work rows, then (256-byte aligned) the argmax summaries.
+size_t sample_scratch_bytes(int64_t V, int rows);
+
 // Tensor parallelism (comm.cu).
 void comm_destroy(BeaconCudaContext* ctx);
 void comm_all_reduce_sum(BeaconCudaContext* ctx, float* buf, size_t count, cudaStream_t s);

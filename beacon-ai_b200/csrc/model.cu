@@ -198,6 +198,8 @@ struct BeaconCudaModel {
     std::unique_ptr<bc::DeviceBuffer> argmax_buf;
     bool pdl = true;  // programmatic dependent launch between the step's kernels
     bc::ArgmaxSummary* argmax_scratch = nullptr;
+    // device sampling: [work rows | argmax summaries | uniforms | previous tokens | next tokens]
+    std::unique_ptr<bc::DeviceBuffer> samp_buf;
     // host staging (pinned)
     int32_t* h_stage = nullptr;  // [0] = position, [1..] tokens
     int32_t* h_next = nullptr;
@@ -983,6 +985,61 @@ int32_t beacon_cuda_model_decode_step(BeaconCudaModel* m, BeaconCudaStream* stre
         check_err(m, s);  // synchronises the stream
         if (next_tokens)
             for (int i = 0; i < batch; ++i) next_tokens[i] = (uint32_t)m->h_next[i];
+        return BEACON_CUDA_OK;
+    });
+}
+
+int32_t beacon_cuda_model_decode_step_sampled(BeaconCudaModel* m, BeaconCudaStream* stream, const uint32_t* tokens,
+                                              int32_t batch, int32_t position, const BeaconCudaSamplingParams* params,
+                                              const float* uniforms, const uint32_t* previous, int32_t n_prev,
+                                              uint32_t* next_tokens) {
+    return guard([&]() -> int32_t {
+        require(m && stream && tokens && params && uniforms && next_tokens, "model_decode_step_sampled: null argument");
+        require(n_prev >= 0 && (n_prev == 0 || previous), "model_decode_step_sampled: previous tokens missing");
+        set_device(m->ctx);
+        check_ready(m);
+        const auto& c = m->cfg;
+        if (batch <= 0 || batch > c.max_batch) invalid("model_decode_step_sampled: batch out of range");
+        if (position < 0 || position + 1 > c.max_context)
+            fail(BEACON_CUDA_ERR_CONTEXT_OVERFLOW, "context overflow: KV cache exhausted");
+        for (int i = 0; i < batch; ++i)
+            if (tokens[i] >= (uint32_t)c.vocab_size) shape_err("embedding index out of bounds for the vocabulary");
+        if (params->has_top_k && params->top_k < 0) invalid("model_decode_step_sampled: top_k must be >= 0");
+        if (!(params->repeat_penalty > 0.0f)) invalid("model_decode_step_sampled: repeat_penalty must be positive");
+        const int64_t V = c.vocab_size;
+        const size_t work = (sample_scratch_bytes(V, batch) + 255) / 256 * 256;
+        const size_t need = work + (size_t)batch * 4 * (2 + (size_t)n_prev) + 256;
+        if (!m->samp_buf || m->samp_buf->bytes < need) {
+            BC_CUDA(cudaStreamSynchronize(stream->s));
+            m->samp_buf = std::make_unique<DeviceBuffer>(need);
+        }
+        uint8_t* base = static_cast<uint8_t*>(m->samp_buf->ptr);
+        float* d_work = reinterpret_cast<float*>(base);
+        auto* d_am = reinterpret_cast<ArgmaxSummary*>(base + ((size_t)batch * V * 4 + 255) / 256 * 256);
+        float* d_unif = reinterpret_cast<float*>(base + work);
+        int32_t* d_prev = reinterpret_cast<int32_t*>(d_unif + batch);
+        int32_t* d_next = d_prev + (size_t)batch * n_prev;
+        cudaStream_t s = stream->s;
+        m->h_stage[0] = position;
+        for (int i = 0; i < batch; ++i) m->h_stage[1 + i] = (int32_t)tokens[i];
+        BC_CUDA(cudaMemcpyAsync(m->pos_dev, m->h_stage, 4, cudaMemcpyHostToDevice, s));
+        BC_CUDA(cudaMemcpyAsync(m->tok, m->h_stage + 1, (size_t)batch * 4, cudaMemcpyHostToDevice, s));
+        BC_CUDA(cudaMemcpyAsync(d_unif, uniforms, (size_t)batch * 4, cudaMemcpyHostToDevice, s));
+        if (n_prev)
+            BC_CUDA(cudaMemcpyAsync(d_prev, previous, (size_t)batch * n_prev * 4, cudaMemcpyHostToDevice, s));
+        if (!c.kv_persist) {
+            const size_t kvb = (size_t)c.max_batch * c.max_context * m->kd * (c.kv_dtype == BEACON_CUDA_DTYPE_F16 ? 2 : 4);
+            for (auto& L : m->layers) {
+                BC_CUDA(cudaMemsetAsync(L.kc->ptr, 0, kvb, s));
+                BC_CUDA(cudaMemsetAsync(L.vc->ptr, 0, kvb, s));
+            }
+        }
+        launch_decode_graph(m, batch, false, s);
+        launch_sample(full_logits(m), V, V, batch, n_prev ? d_prev : nullptr, n_prev, *params, d_unif, d_work, d_next,
+                      d_am, s);
+        BC_CUDA(cudaMemcpyAsync(m->h_next, d_next, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
+        check_err(m, s);  // synchronises the stream
+        for (int i = 0; i < batch; ++i) next_tokens[i] = (uint32_t)m->h_next[i];
         return BEACON_CUDA_OK;
     });
 }

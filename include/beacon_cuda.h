@@ -225,6 +225,31 @@ int32_t beacon_cuda_profile_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaS
                                              const BeaconCudaTensor* const* w, int32_t n_w,
                                              const BeaconCudaTensor* x, int32_t iters, float* out_avg_us,
                                              uint64_t* out_bytes);
+/* The sampling fields of GenerationParams (crates/beacon-scheduler/src/
+ * params.rs:6-31); has_top_k / has_top_p / has_min_p stand for Some(.) of the
+ * Option fields (Some(0) top_k and Some(p) with p >= 1 keep their reference
+ * meaning). */
+typedef struct {
+    float temperature;     /* <= f32::EPSILON: greedy argmax after the penalty */
+    int32_t has_top_k, top_k;
+    int32_t has_top_p;
+    float top_p;
+    int32_t has_min_p;
+    float min_p;
+    float repeat_penalty;  /* 1.0: none */
+} BeaconCudaSamplingParams;
+/* sampling::sample (crates/beacon-scheduler/src/sampling.rs:15-57) per row
+ * of logits [rows, V] F32: repeat penalty over previous_tokens (I32
+ * [rows, n], NULL = none), temperature, top-k, top-p, min-p, softmax and the
+ * multinomial draw with uniforms[row] (F32 [rows], values in [0, 1)) in place
+ * of the reference's rng.random::<f32>(). out: I32 [rows]. The logits are
+ * not modified. Cumulative sums run in parallel (exact fixed-point sums of
+ * the f32 probabilities), so a draw within rounding of a cumulative boundary
+ * may land on the neighbouring token; everything else matches the reference. */
+int32_t beacon_cuda_op_sample(BeaconCudaContext* ctx, BeaconCudaStream* stream,
+                              const BeaconCudaTensor* logits, const BeaconCudaTensor* previous_tokens,
+                              const BeaconCudaSamplingParams* params, const BeaconCudaTensor* uniforms,
+                              BeaconCudaTensor** out);
 /* dequantize_to_f16 (dequant.rs:33-60), bit-exact: out F16 [N, K]. */
 int32_t beacon_cuda_op_dequantize_to_f16(BeaconCudaContext* ctx, BeaconCudaStream* stream,
                                          const BeaconCudaTensor* w, BeaconCudaTensor** out);
@@ -301,6 +326,17 @@ int32_t beacon_cuda_model_forward(BeaconCudaModel* model, BeaconCudaStream* stre
 int32_t beacon_cuda_model_decode_step(BeaconCudaModel* model, BeaconCudaStream* stream,
                                       const uint32_t* tokens, int32_t batch, int32_t position,
                                       uint32_t* next_tokens, float* logits_out);
+/* One decode step whose next tokens are sampled on the device with `params`
+ * (beacon_cuda_op_sample): the host sends tokens [batch], uniforms [batch]
+ * (the draws, in [0, 1)) and previous [batch][n_prev] generated tokens for
+ * the repeat penalty (NULL / 0 = none) and receives next_tokens [batch]; the
+ * logits stay on the device. The CLI's generation loop
+ * (crates/beacon-cli/src/main.rs:306-333) without its per-step logits copy. */
+int32_t beacon_cuda_model_decode_step_sampled(BeaconCudaModel* model, BeaconCudaStream* stream,
+                                              const uint32_t* tokens, int32_t batch, int32_t position,
+                                              const BeaconCudaSamplingParams* params, const float* uniforms,
+                                              const uint32_t* previous, int32_t n_prev,
+                                              uint32_t* next_tokens);
 /* Same step with device buffers (int32 tokens in, int32 next tokens out,
  * logits F32 [batch, vocab] or NULL); enqueued only, nothing is copied.
  * Device-side errors of enqueued steps (context overflow, bounded waits that

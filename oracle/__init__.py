@@ -81,6 +81,7 @@ def lib() -> ctypes.CDLL:
             "orc_attention": (c.c_int, [P, P, P, P, c.c_size_t, c.c_float, c.c_size_t, c.c_size_t,
                                         c.c_size_t, c.c_size_t, c.c_size_t, c.c_size_t, c.c_int, P]),
             "orc_argmax": (c.c_uint32, [P, c.c_size_t]),
+            "orc_sample": (c.c_uint32, [P, c.c_size_t, P, c.c_size_t, P, c.c_float, P]),
             "orc_model_create": (P, [P]),
             "orc_model_set_weight": (c.c_int, [P, c.c_int, c.c_int, P, c.c_int, c.c_int]),
             "orc_model_forward": (c.c_int, [P, P, c.c_size_t, c.c_size_t, P]),
@@ -305,6 +306,29 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
 def argmax(logits: np.ndarray) -> int:
     x = np.ascontiguousarray(logits, dtype=np.float32)
     return int(lib().orc_argmax(_p(x), x.size))
+
+
+class SampleParams(ctypes.Structure):
+    """GenerationParams' sampling fields (params.rs:6-31); has_* = Some(.)."""
+    _fields_ = [("temperature", ctypes.c_float), ("has_top_k", ctypes.c_int32), ("top_k", ctypes.c_int32),
+                ("has_top_p", ctypes.c_int32), ("top_p", ctypes.c_float), ("has_min_p", ctypes.c_int32),
+                ("min_p", ctypes.c_float), ("repeat_penalty", ctypes.c_float)]
+
+
+def sample_params(temperature=0.0, top_k=None, top_p=None, min_p=None, repeat_penalty=1.0) -> SampleParams:
+    return SampleParams(temperature, top_k is not None, top_k or 0, top_p is not None,
+                        0.0 if top_p is None else top_p, min_p is not None, 0.0 if min_p is None else min_p,
+                        repeat_penalty)
+
+
+def sample(logits: np.ndarray, previous, params: SampleParams, r: float):
+    """sampling::sample (sampling.rs:15-57) with the draw r given: (token, final distribution)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    prev = np.ascontiguousarray(np.asarray(previous, dtype=np.uint32))
+    probs = np.zeros(x.size, dtype=np.float32)
+    tok = lib().orc_sample(_p(x), x.size, _p(prev) if prev.size else None, prev.size, ctypes.byref(params),
+                           r, _p(probs))
+    return int(tok), probs
 
 
 class _Cfg(ctypes.Structure):

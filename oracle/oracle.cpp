@@ -945,3 +945,101 @@ extern "C" int orc_model_forward(void* model, const uint32_t* tokens, size_t S, 
 }
 
 extern "C" const char* orc_last_error(void) { return g_err.c_str(); }
+
+// ---------------------------------------------------------------------------
+// Sampling pipeline (crates/beacon-scheduler/src/sampling.rs:15-186):
+// repeat penalty -> temperature (greedy at <= f32::EPSILON) -> top-k -> top-p
+// -> min-p -> softmax -> multinomial draw. The reference draws
+// r = rng.random::<f32>() from an unseeded thread RNG; here r is an input so
+// that the draw can be replayed. The stages run in the reference's order and
+// its f32 arithmetic (sequential sums in index order, sort by descending
+// value). probs_out (optional, n floats): the distribution the draw used.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+const float kF32Eps = 1.1920929e-07f;  // f32::EPSILON
+
+// sampling.rs:173-186 (softmax_inplace)
+void sample_softmax(std::vector<float>& x) {
+    float mx = -INFINITY;
+    for (float v : x) mx = std::fmax(mx, v);  // fold(NEG_INFINITY, f32::max)
+    float sum = 0.0f;
+    for (float& v : x) {
+        v = std::exp(v - mx);
+        sum += v;
+    }
+    if (sum > 0.0f) {
+        const float inv = 1.0f / sum;
+        for (float& v : x) v *= inv;
+    }
+}
+
+// partial_cmp(a, b).unwrap_or(Equal) == Greater, i.e. a > b without NaN
+bool desc_before(float a, float b) { return a > b; }
+
+}  // namespace
+
+extern "C" uint32_t orc_sample(const float* logits_in, size_t n, const uint32_t* prev, size_t n_prev,
+                               const OrcSampleParams* p, float r, float* probs_out) {
+    std::vector<float> logits(logits_in, logits_in + n);
+    // 1. repeat penalty (sampling.rs:77-88), once per occurrence
+    if (std::fabs(p->repeat_penalty - 1.0f) > kF32Eps) {
+        for (size_t i = 0; i < n_prev; ++i) {
+            const size_t idx = prev[i];
+            if (idx < n) logits[idx] = logits[idx] > 0.0f ? logits[idx] / p->repeat_penalty
+                                                          : logits[idx] * p->repeat_penalty;
+        }
+    }
+    // 2. temperature (sampling.rs:27-34, 91-96)
+    if (p->temperature <= kF32Eps) return orc_argmax(logits.data(), n);
+    if (std::fabs(p->temperature - 1.0f) > kF32Eps) {
+        const float inv_t = 1.0f / p->temperature;
+        for (float& v : logits) v *= inv_t;
+    }
+    // 3. top-k (sampling.rs:99-114): threshold = sorted_desc[k], drop v < threshold
+    if (p->has_top_k && (size_t)p->top_k < n) {
+        std::vector<float> sorted(logits);
+        std::sort(sorted.begin(), sorted.end(), desc_before);
+        const float threshold = sorted[(size_t)p->top_k];
+        for (float& v : logits)
+            if (v < threshold) v = -INFINITY;
+    }
+    // 4. top-p (sampling.rs:117-145)
+    if (p->has_top_p && p->top_p < 1.0f) {
+        std::vector<float> probs(logits);
+        sample_softmax(probs);
+        std::vector<size_t> idx(n);
+        for (size_t i = 0; i < n; ++i) idx[i] = i;
+        std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return probs[a] > probs[b]; });
+        float cumulative = 0.0f;
+        size_t cutoff = n;
+        for (size_t i = 0; i < n; ++i) {
+            cumulative += probs[idx[i]];
+            if (cumulative > p->top_p) {
+                cutoff = i + 1;
+                break;
+            }
+        }
+        for (size_t i = cutoff; i < n; ++i) logits[idx[i]] = -INFINITY;
+    }
+    // 5. min-p (sampling.rs:148-160)
+    if (p->has_min_p && p->min_p > 0.0f) {
+        std::vector<float> probs(logits);
+        sample_softmax(probs);
+        float max_prob = 0.0f;
+        for (float v : probs) max_prob = std::fmax(max_prob, v);
+        const float threshold = p->min_p * max_prob;
+        for (size_t i = 0; i < n; ++i)
+            if (probs[i] < threshold) logits[i] = -INFINITY;
+    }
+    // 6. softmax + multinomial (sampling.rs:53-56, 163-186)
+    sample_softmax(logits);
+    if (probs_out) std::memcpy(probs_out, logits.data(), n * sizeof(float));
+    float cumulative = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        cumulative += logits[i];
+        if (cumulative >= r) return (uint32_t)i;
+    }
+    return n ? (uint32_t)(n - 1) : 0u;
+}

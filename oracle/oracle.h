@@ -81,6 +81,21 @@ int  orc_attention(const float* q, const float* k, const float* v,
                    int causal, float* out);
 uint32_t orc_argmax(const float* logits, size_t n);
 
+/* GenerationParams' sampling fields (crates/beacon-scheduler/src/params.rs:6-31);
+ * the has_* flags stand for Some(.) of the Option fields. */
+typedef struct {
+    float temperature;
+    int32_t has_top_k, top_k;
+    int32_t has_top_p;
+    float top_p;
+    int32_t has_min_p;
+    float min_p;
+    float repeat_penalty;
+} OrcSampleParams;
+/* sampling.rs:15-57 with the draw r in [0, 1) given. */
+uint32_t orc_sample(const float* logits, size_t n, const uint32_t* prev, size_t n_prev,
+                    const OrcSampleParams* p, float r, float* probs_out);
+
 /* Llama-style engine (crates/beacon-core/src/engine.rs:190-456). */
 typedef struct {
     int32_t vocab_size, hidden_size, num_layers, num_heads, num_kv_heads;

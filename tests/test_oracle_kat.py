@@ -354,3 +354,61 @@ def test_engine_context_overflow():  # engine.rs:366-368
     m = build_oracle_model(cfg, make_weights(cfg, orc.Q4_0, seed=1))
     with pytest.raises(RuntimeError, match="overflow"):
         m.forward([1, 2, 3, 4, 5], 0)
+
+
+# --- sampling (crates/beacon-scheduler/src/tests.rs:10-75) -----------------------------
+
+def test_sample_greedy_kat():
+    """tests.rs:11-20: temperature 0 picks the highest logit."""
+    assert orc.sample([1.0, 3.0, 2.0, 0.5], [], orc.sample_params(0.0), 0.5)[0] == 1
+
+
+def test_sample_argmax_kat():
+    """tests.rs:23-27."""
+    assert orc.argmax(np.array([1.0, 5.0, 3.0], np.float32)) == 1
+    assert orc.argmax(np.array([9.0, 1.0, 2.0], np.float32)) == 0
+    assert orc.argmax(np.array([0.0, 0.0, 1.0], np.float32)) == 2
+
+
+def test_sample_low_temperature_kat():
+    """tests.rs:30-40: temperature 0.01 behaves like greedy, for any draw."""
+    for r in (1e-6, 0.3, 0.999999):
+        assert orc.sample([1.0, 10.0, 2.0], [], orc.sample_params(0.01), r)[0] == 1
+    # r = 0.0 (rng.random() can return it) takes index 0 whatever its probability: cumulative >= r
+    assert orc.sample([1.0, 10.0, 2.0], [], orc.sample_params(0.01), 0.0)[0] == 0
+
+
+def test_sample_repeat_penalty_kat():
+    """tests.rs:43-57: penalty 2 halves token 1's positive logit (5.0 -> 2.5)."""
+    assert orc.sample([4.9, 5.0, 1.0], [1], orc.sample_params(0.0, repeat_penalty=2.0), 0.5)[0] == 0
+
+
+def test_sample_top_k_kat():
+    """tests.rs:60-75: top_k 2 keeps only tokens 1 and 2."""
+    for r in np.linspace(1e-6, 0.999, 7):
+        assert orc.sample([1.0, 10.0, 5.0, 0.1], [], orc.sample_params(0.001, top_k=2), float(r))[0] in (1, 2)
+
+
+def test_sample_pipeline_definitions():
+    """Values that follow from sampling.rs's definitions: top_k = Some(k) keeps
+    every value >= the k-th largest (0-based), so k = 1 keeps two tokens; top_p
+    keeps the smallest descending prefix whose mass exceeds p; min_p drops
+    probabilities below min_p * max; the draw takes the first index whose
+    cumulative probability reaches r; a repeated token is penalised once per
+    occurrence; negative logits are multiplied by the penalty."""
+    lg = np.log(np.array([0.1, 0.4, 0.2, 0.3], np.float32))
+    _, p = orc.sample(lg, [], orc.sample_params(1.0, top_k=1), 0.5)
+    assert (p > 0).tolist() == [False, True, False, True]
+    _, p = orc.sample(lg, [], orc.sample_params(1.0, top_p=0.65), 0.5)    # 0.4 + 0.3 > 0.65
+    assert (p > 0).tolist() == [False, True, False, True]
+    _, p = orc.sample(lg, [], orc.sample_params(1.0, min_p=0.6), 0.5)     # 0.4 * 0.6 = 0.24: keeps 0.3, 0.4
+    assert (p > 0).tolist() == [False, True, False, True]
+    probs = np.array([0.1, 0.4, 0.2, 0.3], np.float32)
+    assert orc.sample(lg, [], orc.sample_params(1.0), 0.05)[0] == 0
+    assert orc.sample(lg, [], orc.sample_params(1.0), 0.45)[0] == 1
+    assert orc.sample(lg, [], orc.sample_params(1.0), 0.65)[0] == 2
+    assert orc.sample(lg, [], orc.sample_params(1.0), 0.95)[0] == 3
+    _, p2 = orc.sample(lg, [1, 1], orc.sample_params(1.0, repeat_penalty=2.0), 0.5)
+    _, p1 = orc.sample(lg, [1], orc.sample_params(1.0, repeat_penalty=4.0), 0.5)
+    assert np.allclose(p2, p1, rtol=0, atol=1e-7)     # log(0.4) < 0: *2 *2 == *4
+    assert np.isclose(probs.sum(), 1.0)
