@@ -27,9 +27,14 @@ namespace bc {
 
 enum { FMT_Q4_0 = 0, FMT_Q8_0 = 1, FMT_Q4_K = 2 };
 
+}  // namespace bc
+#include "gemv_generic.cuh"
+namespace bc {
+
+// 16-byte chunks per row per tile after the first (the meta chunk)
 template <int FMT>
 struct Fmt {
-    static constexpr int CH = (FMT == FMT_Q8_0) ? 16 : 8;  // 16-byte chunks per row per tile
+    static constexpr int CH = FMT == FMT_Q8_0 ? 16 : FMT <= FMT_Q4_K ? 8 : GenericFmt<FMT>::CHUNKS - 1;
 };
 
 struct GemvParams {
@@ -416,6 +421,33 @@ __device__ __forceinline__ void consume_q4_k(const uint4& meta, const uint4 (&q)
     }
 }
 
+// Generic formats (gemv_generic.cuh): the row slice (meta chunk + CH chunks)
+// decoded from registers to the reference's f32 weights (f16-truncated for
+// the CPU-reproducing numerics) against f32 activations staged in shared
+// memory.
+template <int FMT, int B>
+__device__ __forceinline__ void consume_generic(const uint4& meta, const uint4* q, const uint8_t* smem, int span,
+                                                int tile, float (&acc)[B], bool rtz) {
+    uint32_t w[GenericFmt<FMT>::WORDS];
+    w[0] = meta.x;
+    w[1] = meta.y;
+    w[2] = meta.z;
+    w[3] = meta.w;
+#pragma unroll
+    for (int c = 0; c < GenericFmt<FMT>::CHUNKS - 1; ++c) {
+        w[4 + 4 * c] = q[c].x;
+        w[5 + 4 * c] = q[c].y;
+        w[6 + 4 * c] = q[c].z;
+        w[7 + 4 * c] = q[c].w;
+    }
+    const float* xs = reinterpret_cast<const float*>(smem) + tile * 256;
+    decode_slice<FMT, false>(w, [&](int e, float v) {
+        if (rtz) v = f16_round_trip_rtz(v);
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] = fmaf(v, xs[(size_t)b * span + e], acc[b]);
+    });
+}
+
 // Epilogue --------------------------------------------------------------------
 // The SwiGLU outputs of row groups 2j and 2j+1 form the 32-element block j of
 // the next GEMV's input: the second of the two groups to finish (an
@@ -564,12 +596,14 @@ __global__ void __launch_bounds__(128) qgemv_kernel(const GemvParams p, const in
         uint4 q[CH];
 #pragma unroll
         for (int c = 0; c < CH; ++c) q[c] = ldg_stream(reinterpret_cast<const uint4*>(tp + 512 + c * 512) + lane);
-        if (FMT == FMT_Q4_0)
+        if constexpr (FMT == FMT_Q4_0)
             consume_q4_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), smem, span, t, acc, rtz);
-        else if (FMT == FMT_Q8_0)
+        else if constexpr (FMT == FMT_Q8_0)
             consume_q8_0<MODE, B>(meta, *reinterpret_cast<uint4(*)[16]>(q), smem, span, t, acc, rtz);
-        else
+        else if constexpr (FMT == FMT_Q4_K)
             consume_q4_k<MODE, B>(meta, *reinterpret_cast<uint4(*)[8]>(q), smem, span, t, acc, rtz);
+        else
+            consume_generic<FMT, B>(meta, q, smem, span, t, acc, rtz);
     }
 #pragma unroll
     for (int b = 0; b < B; ++b) red[warp][b][lane] = acc[b];
@@ -649,13 +683,17 @@ void launch_qgemv_t(const GemvLaunch& a) {
 template <int FMT>
 void launch_qgemv_fmt(const GemvLaunch& a) {
     const int bp = a.plan->bpad;
-    if (a.mode == MODE_FAST) {
-        switch (bp) {
-            case 1: return launch_qgemv_t<FMT, MODE_FAST, 1>(a);
-            case 2: return launch_qgemv_t<FMT, MODE_FAST, 2>(a);
-            case 4: return launch_qgemv_t<FMT, MODE_FAST, 4>(a);
-            case 8: return launch_qgemv_t<FMT, MODE_FAST, 8>(a);
-            default: return launch_qgemv_t<FMT, MODE_FAST, 16>(a);
+    // the generic formats always compute in f32 (their slices decode to the
+    // reference's f32 values; there is no integer fast path for them)
+    if constexpr (FMT <= FMT_Q4_K) {
+        if (a.mode == MODE_FAST) {
+            switch (bp) {
+                case 1: return launch_qgemv_t<FMT, MODE_FAST, 1>(a);
+                case 2: return launch_qgemv_t<FMT, MODE_FAST, 2>(a);
+                case 4: return launch_qgemv_t<FMT, MODE_FAST, 4>(a);
+                case 8: return launch_qgemv_t<FMT, MODE_FAST, 8>(a);
+                default: return launch_qgemv_t<FMT, MODE_FAST, 16>(a);
+            }
         }
     }
     switch (bp) {

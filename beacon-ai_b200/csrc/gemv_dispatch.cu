@@ -11,6 +11,7 @@ namespace bc {
 
 GemvPlan plan_qgemv(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
     if (batch < 1 || batch > 16) invalid("quantized GEMV supports batch 1..16");
+    if (!is_core_format(L.dtype)) mode = MODE_F32;  // generic formats stage f32 activations
     GemvPlan pl;
     pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16;
     const int64_t groups = L.groups(), ktiles = L.ktiles();
@@ -41,10 +42,22 @@ void launch_qgemv(const GemvPlan& plan, const QLayout& L, const void* w, const v
             invalid("split-K GEMV launched without enough scratch");
     }
     GemvLaunch a{&plan, &L, w, x, x_f16, x_ld, batch, y, y_ld, epi, res, res_ld, mode, rtz, scratch, s};
-    switch (L.dtype) {
+    launch_qgemv_any(a);
+}
+
+void launch_qgemv_any(const GemvLaunch& a) {
+    switch (a.L->dtype) {
         case BEACON_CUDA_DTYPE_Q4_0: return launch_qgemv_q4_0(a);
         case BEACON_CUDA_DTYPE_Q8_0: return launch_qgemv_q8_0(a);
         case BEACON_CUDA_DTYPE_Q4_K: return launch_qgemv_q4_k(a);
+        case BEACON_CUDA_DTYPE_Q4_1: return launch_qgemv_q4_1(a);
+        case BEACON_CUDA_DTYPE_Q5_0: return launch_qgemv_q5_0(a);
+        case BEACON_CUDA_DTYPE_Q5_1: return launch_qgemv_q5_1(a);
+        case BEACON_CUDA_DTYPE_Q2_K: return launch_qgemv_q2_k(a);
+        case BEACON_CUDA_DTYPE_Q3_K: return launch_qgemv_q3_k(a);
+        case BEACON_CUDA_DTYPE_Q5_K: return launch_qgemv_q5_k(a);
+        case BEACON_CUDA_DTYPE_Q6_K: return launch_qgemv_q6_k(a);
+        case BEACON_CUDA_DTYPE_Q8_K: return launch_qgemv_q8_k(a);
         default: fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized GEMV: unsupported block type");
     }
 }
@@ -74,7 +87,7 @@ constexpr size_t kSpreadSmem = 117 * 1024;
 LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch, int mode) {
     LinearPlan pl;
     pl.v2 = plan_qgemv(ctx, L, batch, mode);
-    if (batch > 8) return pl;
+    if (batch > 8 || !is_core_format(L.dtype)) return pl;  // the persistent kernel serves the dedicated layouts
     pl.bpad = batch <= 1 ? 1 : batch <= 2 ? 2 : batch <= 4 ? 4 : 8;
     const size_t budget = 220 * 1024, half_sm = 110 * 1024;
     // The fast numerics consume tiles with the tensor-core (mma.sync) consumer
@@ -187,12 +200,7 @@ void launch_linear(const LinearPlan& plan, const QLayout& L, const void* w, cons
             (!scratch.partial || !scratch.counters || scratch.partial_floats < (size_t)plan.v2.ksplit * batch * L.n_pad ||
              scratch.counter_count < L.groups()))
             invalid("split-K GEMV launched without enough scratch");
-        switch (L.dtype) {
-            case BEACON_CUDA_DTYPE_Q4_0: return launch_qgemv_q4_0(a);
-            case BEACON_CUDA_DTYPE_Q8_0: return launch_qgemv_q8_0(a);
-            case BEACON_CUDA_DTYPE_Q4_K: return launch_qgemv_q4_k(a);
-            default: fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized GEMV: unsupported block type");
-        }
+        return launch_qgemv_any(a);
     }
     if (!scratch.partial || !scratch.counters || !scratch.err ||
         scratch.partial_floats < plan.scratch_floats(batch, L) || scratch.counter_count < L.groups())

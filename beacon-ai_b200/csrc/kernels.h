@@ -138,6 +138,21 @@ void allow_max_dynamic_smem(void (*kern)(KArgs...)) {
 void launch_qgemv_q4_0(const GemvLaunch& a);
 void launch_qgemv_q8_0(const GemvLaunch& a);
 void launch_qgemv_q4_k(const GemvLaunch& a);
+// Formats with a dedicated tile layout and integer fast path (the others
+// keep raw block bytes per tile and compute in f32, gemv_generic.cuh).
+inline bool is_core_format(int32_t dtype) {
+    return dtype == BEACON_CUDA_DTYPE_Q4_0 || dtype == BEACON_CUDA_DTYPE_Q8_0 || dtype == BEACON_CUDA_DTYPE_Q4_K;
+}
+void launch_qgemv_q4_1(const GemvLaunch& a);
+void launch_qgemv_q5_0(const GemvLaunch& a);
+void launch_qgemv_q5_1(const GemvLaunch& a);
+void launch_qgemv_q2_k(const GemvLaunch& a);
+void launch_qgemv_q3_k(const GemvLaunch& a);
+void launch_qgemv_q5_k(const GemvLaunch& a);
+void launch_qgemv_q6_k(const GemvLaunch& a);
+void launch_qgemv_q8_k(const GemvLaunch& a);
+// The tiled kernel of any block format.
+void launch_qgemv_any(const GemvLaunch& a);
 
 // The persistent TMA-fed GEMV (gemv3.cuh) for batch <= 8 when its ring and the
 // staged activations fit in shared memory; otherwise the tiled GEMV above.

@@ -4,7 +4,13 @@
 //    (crates/beacon-format/src/dequant.rs:33-60, 160-178, 258-273, 289-365);
 //  * quantize: f32 -> GGUF blocks with the deterministic fixture quantizer
 //    (the reference has none; the CPU oracle writes identical bytes).
+// The other block types (Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, Q6_K, Q8_K,
+// dequant.rs:182-254, 377-597) keep their raw bytes per tile
+// (gemv_generic.cuh).
+#include <algorithm>
+
 #include "common.cuh"
+#include "gemv_generic.cuh"
 #include "internal.h"
 #include "kernels.h"
 
@@ -265,12 +271,82 @@ __global__ void quantize_kernel(const float* __restrict__ x, uint8_t* __restrict
 
 inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
 
+// Generic formats (gemv_generic.cuh): tile t of row r holds the raw bytes of
+// the row's 256 columns [256 t, 256 t + 256), zero-padded to whole chunks.
+// One thread per (tiled row, k-tile); row_map as for repack_kernel.
+__global__ void repack_generic_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ tiled, int64_t n,
+                                      int64_t row_bytes, int64_t slice, int64_t n_pad, int64_t ktiles,
+                                      int64_t tile_bytes, int chunks_total, const int64_t* __restrict__ row_map) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_pad * ktiles) return;
+    const int64_t r = idx / ktiles, t = idx - r * ktiles;
+    int64_t src_row = r < n ? r : -1;
+    if (row_map) {
+        src_row = row_map[r];
+        if (src_row == -2) return;
+    }
+    const int64_t g = r / 32, lane = r % 32;
+    uint8_t* base = tiled + (g * ktiles + t) * tile_bytes + lane * 16;
+    const int64_t off = t * slice;
+    const int64_t avail = src_row >= 0 ? std::max<int64_t>(0, std::min<int64_t>(slice, row_bytes - off)) : 0;
+    const uint8_t* src = src_row >= 0 ? raw + src_row * row_bytes + off : nullptr;
+    for (int c = 0; c < chunks_total; ++c) {
+        uint8_t b[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int64_t j = (int64_t)c * 16 + i;
+            b[i] = j < avail ? src[j] : 0;
+        }
+        store16(base + (int64_t)c * 512, b);
+    }
+}
+
+// Generic formats: one thread per (row, k-tile), 256 f16 values (fewer in a
+// ragged last tile), bit-exact with dequantize_to_f16.
+template <int FMT>
+__global__ void dequant_generic_kernel(const uint8_t* __restrict__ tiled, uint16_t* __restrict__ out, int64_t n,
+                                       int64_t k, int64_t ktiles, int64_t tile_bytes) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n * ktiles) return;
+    const int64_t r = idx / ktiles, t = idx - r * ktiles;
+    const uint8_t* base = tiled + ((r / 32) * ktiles + t) * tile_bytes + (r % 32) * 16;
+    uint32_t w[GenericFmt<FMT>::WORDS];
+#pragma unroll
+    for (int c = 0; c < GenericFmt<FMT>::CHUNKS; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(base + c * 512);
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+    }
+    const int64_t c0 = t * 256, ncol = std::min<int64_t>(256, k - c0);
+    uint16_t* o = out + r * k + c0;
+    decode_slice<FMT, true>(w, [&](int e, float v) {
+        if (e < ncol) o[e] = f32_to_f16_rtz(v);
+    });
+}
+
+template <int FMT>
+void launch_dequant_generic(const QLayout& L, const uint8_t* tiled, uint16_t* out, cudaStream_t s) {
+    const int64_t total = L.n * L.ktiles();
+    dequant_generic_kernel<FMT><<<blocks_for(total, 64), 64, 0, s>>>(tiled, out, L.n, L.k, L.ktiles(), L.tile_bytes);
+    BC_LAUNCHED("dequant_generic_kernel");
+}
+
 }  // namespace
 
 void launch_repack(const QLayout& L, const uint8_t* raw, int nibble_order, uint8_t* tiled,
                    const int64_t* row_map, cudaStream_t s) {
     const int64_t total = L.n_pad * L.ktiles();
     if (total == 0) return;
+    if (!is_core_format(L.dtype)) {
+        const int64_t row_bytes = L.k / block_size(L.dtype) * block_bytes(L.dtype);
+        const int64_t slice = 256 / block_size(L.dtype) * block_bytes(L.dtype);
+        repack_generic_kernel<<<blocks_for(total, 128), 128, 0, s>>>(raw, tiled, L.n, row_bytes, slice, L.n_pad,
+                                                                     L.ktiles(), L.tile_bytes, L.chunks + 1, row_map);
+        BC_LAUNCHED("repack_generic_kernel");
+        return;
+    }
     repack_kernel<<<blocks_for(total, 128), 128, 0, s>>>(
         raw, tiled, L.dtype, L.n, L.k, L.n_pad, L.ktiles(), L.tile_bytes, L.chunks,
         nibble_order == BEACON_CUDA_NIBBLE_GGUF_SPLIT ? 1 : 0, row_map);
@@ -278,6 +354,18 @@ void launch_repack(const QLayout& L, const uint8_t* raw, int nibble_order, uint8
 }
 
 void launch_dequant_f16(const QLayout& L, const uint8_t* tiled, uint16_t* out, cudaStream_t s) {
+    if (L.n == 0) return;
+    switch (L.dtype) {
+        case BEACON_CUDA_DTYPE_Q4_1: return launch_dequant_generic<FMT_Q4_1>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q5_0: return launch_dequant_generic<FMT_Q5_0>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q5_1: return launch_dequant_generic<FMT_Q5_1>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q2_K: return launch_dequant_generic<FMT_Q2_K>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q3_K: return launch_dequant_generic<FMT_Q3_K>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q5_K: return launch_dequant_generic<FMT_Q5_K>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q6_K: return launch_dequant_generic<FMT_Q6_K>(L, tiled, out, s);
+        case BEACON_CUDA_DTYPE_Q8_K: return launch_dequant_generic<FMT_Q8_K>(L, tiled, out, s);
+        default: break;
+    }
     const int64_t total = L.n * (L.k / 32);
     if (total == 0) return;
     dequant_f16_kernel<<<blocks_for(total, 128), 128, 0, s>>>(tiled, out, L.dtype, L.n, L.k,

@@ -64,9 +64,19 @@ size_t plain_elem_bytes(int32_t dtype) {
     }
 }
 
-static bool gemv_supported(int32_t dtype) {
-    return dtype == BEACON_CUDA_DTYPE_Q4_0 || dtype == BEACON_CUDA_DTYPE_Q8_0 ||
-           dtype == BEACON_CUDA_DTYPE_Q4_K;
+static bool gemv_supported(int32_t dtype) { return is_quantized(dtype); }
+
+// Nominal bits per weight code of each block type (the `bits` argument of
+// quantized_matmul, backend.rs:32-41).
+static int code_bits(int32_t dtype) {
+    switch (dtype) {
+        case BEACON_CUDA_DTYPE_Q2_K: return 2;
+        case BEACON_CUDA_DTYPE_Q3_K: return 3;
+        case BEACON_CUDA_DTYPE_Q5_0: case BEACON_CUDA_DTYPE_Q5_1: case BEACON_CUDA_DTYPE_Q5_K: return 5;
+        case BEACON_CUDA_DTYPE_Q6_K: return 6;
+        case BEACON_CUDA_DTYPE_Q8_0: case BEACON_CUDA_DTYPE_Q8_K: return 8;
+        default: return 4;
+    }
 }
 
 QLayout make_qlayout(int32_t dtype, int64_t n, int64_t k) {
@@ -81,7 +91,13 @@ QLayout make_qlayout(int32_t dtype, int64_t n, int64_t k) {
     L.k = k;
     L.n_pad = (n + 31) / 32 * 32;
     L.k_pad = (k + 255) / 256 * 256;
-    L.chunks = dtype == BEACON_CUDA_DTYPE_Q8_0 ? 16 : 8;
+    if (is_core_format(dtype)) {
+        L.chunks = dtype == BEACON_CUDA_DTYPE_Q8_0 ? 16 : 8;
+    } else {
+        // raw bytes of 256 columns, in 16-byte chunks (the first is the "meta" chunk)
+        const int64_t slice = 256 / block_size(dtype) * block_bytes(dtype);
+        L.chunks = (int32_t)((slice + 15) / 16 - 1);
+    }
     L.tile_bytes = 32 * (16 + 16 * (int64_t)L.chunks);
     return L;
 }
@@ -551,7 +567,7 @@ int32_t beacon_cuda_op_quantized_matmul(BeaconCudaContext* ctx, BeaconCudaStream
         require(ctx && stream && x && w && out, "beacon_cuda_op_quantized_matmul: null argument");
         if (!is_quantized(w->dtype)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "quantized_matmul: w is not quantized");
         const int exp_gs = (int)block_size(w->dtype);
-        const int exp_bits = w->dtype == BEACON_CUDA_DTYPE_Q8_0 ? 8 : 4;
+        const int exp_bits = code_bits(w->dtype);
         if ((group_size != 0 && group_size != exp_gs) || (bits != 0 && bits != exp_bits))
             invalid("quantized_matmul: group_size/bits disagree with the weight's block type");
         if (x->dtype != BEACON_CUDA_DTYPE_F32 && x->dtype != BEACON_CUDA_DTYPE_F16)
