@@ -132,6 +132,19 @@ SIGNATURES = {
     "beacon_cuda_model_launches_per_step": (_I32, [_P, _I32, _I32, ctypes.POINTER(_I32)]),
     "beacon_cuda_stream_handle": (_I32, [_P, _PP]),
     "beacon_cuda_model_memory": (_I32, [_P, ctypes.POINTER(ctypes.c_uint64)]),
+    "beacon_cuda_gguf_open": (_I32, [ctypes.c_char_p, _PP]),
+    "beacon_cuda_gguf_close": (None, [_P]),
+    "beacon_cuda_gguf_version": (_I32, [_P, ctypes.POINTER(ctypes.c_uint32)]),
+    "beacon_cuda_gguf_tensor_count": (_I32, [_P, ctypes.POINTER(_I64)]),
+    "beacon_cuda_gguf_tensor_info": (_I32, [_P, _I64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_I32), _P,
+                                            ctypes.POINTER(_SZ), _PP, ctypes.POINTER(ctypes.c_uint64)]),
+    "beacon_cuda_gguf_find_tensor": (_I32, [_P, ctypes.c_char_p, ctypes.POINTER(_I64)]),
+    "beacon_cuda_gguf_get_int": (_I32, [_P, ctypes.c_char_p, ctypes.POINTER(_I64)]),
+    "beacon_cuda_gguf_get_float": (_I32, [_P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    "beacon_cuda_gguf_get_string": (_I32, [_P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)]),
+    "beacon_cuda_gguf_get_array_len": (_I32, [_P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "beacon_cuda_gguf_model_config": (_I32, [_P, _P]),
+    "beacon_cuda_model_load_gguf": (_I32, [_P, _P]),
     "beacon_cuda_comm_unique_id": (_I32, [_P]),
     "beacon_cuda_comm_init": (_I32, [_P, _I32, _I32, _P, _I32]),
     "beacon_cuda_op_all_reduce_f32": (_I32, [_P, _P, _P]),

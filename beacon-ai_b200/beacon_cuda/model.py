@@ -65,6 +65,10 @@ class CudaModel:
             _raise(L.lib().beacon_cuda_model_set_weight(self._h, layer, slot, arr.ctypes.data, dtype,
                                                         nibble_order, 0))
 
+    def load_gguf(self, gguf) -> None:
+        """Every weight slot from a GGUF file (beacon_cuda.gguf.GgufFile)."""
+        _raise(L.lib().beacon_cuda_model_load_gguf(self._h, gguf.handle))
+
     def reset(self) -> None:
         _raise(L.lib().beacon_cuda_model_reset(self._h))
 

@@ -194,6 +194,10 @@ GemvScratch stream_gemv_scratch(BeaconCudaStream* stream, const LinearPlan& pl, 
 void dense_qmatmul(BeaconCudaContext* ctx, BeaconCudaStream* stream, const BeaconCudaTensor* w, const void* x,
                    bool x_f16, int64_t rows, float* out, int numerics);
 
+// The model's configuration and context (model.cu), for the GGUF loader.
+const BeaconCudaModelConfig& model_config_of(const BeaconCudaModel* m);
+BeaconCudaContext* model_context_of(const BeaconCudaModel* m);
+
 // Token sampling (sample.cu): rows of logits [rows][ld] (V used) -> out[rows].
 struct ArgmaxSummary;
 void launch_sample(const float* logits, int64_t ld, int64_t V, int rows, const int32_t* prev, int n_prev,

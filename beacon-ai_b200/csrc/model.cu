@@ -561,6 +561,9 @@ void release_graphs(BeaconCudaModel* m) {
 }  // namespace
 }  // namespace bc
 
+const BeaconCudaModelConfig& bc::model_config_of(const BeaconCudaModel* m) { return m->cfg; }
+BeaconCudaContext* bc::model_context_of(const BeaconCudaModel* m) { return m->ctx; }
+
 BeaconCudaModel::~BeaconCudaModel() {
     bc::release_graphs(this);
     if (h_stage) cudaFreeHost(h_stage);

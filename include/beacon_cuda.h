@@ -373,6 +373,49 @@ int32_t beacon_cuda_stream_handle(BeaconCudaStream* stream, void** out_cuda_stre
 /* Bytes of device memory held by the model (weights + KV cache + workspace). */
 int32_t beacon_cuda_model_memory(const BeaconCudaModel* model, uint64_t* out_bytes);
 
+/* === GGUF v3 files (crates/beacon-format/src/gguf) === */
+typedef struct BeaconCudaGguf BeaconCudaGguf;
+/* GgufFile::open (gguf/mod.rs:39-68): memory-maps the file and parses the
+ * header (header.rs:17-47), the metadata key-value pairs (metadata.rs:133-151)
+ * and the tensor infos, dims reversed to row-major (tensor_info.rs:13-77);
+ * data offsets are resolved against general.alignment (default 32). A bad
+ * magic or an unknown value type is INVALID_ARGUMENT, a version other than 3
+ * or an unknown tensor type UNSUPPORTED_DTYPE, a truncated file
+ * SHAPE_MISMATCH. Needs no GPU. */
+int32_t beacon_cuda_gguf_open(const char* path, BeaconCudaGguf** out);
+void    beacon_cuda_gguf_close(BeaconCudaGguf* f);
+int32_t beacon_cuda_gguf_version(const BeaconCudaGguf* f, uint32_t* out);
+int32_t beacon_cuda_gguf_tensor_count(const BeaconCudaGguf* f, int64_t* out);
+/* Tensor `index`: name (valid while the file is open), BeaconDtype tag (-1
+ * for GGUF types without one), row-major shape, bytes in the mapping
+ * (GgufFile::tensor_data, mod.rs:79-84) and their length. */
+int32_t beacon_cuda_gguf_tensor_info(const BeaconCudaGguf* f, int64_t index, const char** out_name,
+                                     int32_t* out_dtype, int64_t* out_shape, size_t* inout_ndim,
+                                     const void** out_data, uint64_t* out_nbytes);
+int32_t beacon_cuda_gguf_find_tensor(const BeaconCudaGguf* f, const char* name, int64_t* out_index);
+/* Metadata values by key (integers of every width and bools; f32/f64;
+ * strings; array lengths). */
+int32_t beacon_cuda_gguf_get_int(const BeaconCudaGguf* f, const char* key, int64_t* out);
+int32_t beacon_cuda_gguf_get_float(const BeaconCudaGguf* f, const char* key, double* out);
+int32_t beacon_cuda_gguf_get_string(const BeaconCudaGguf* f, const char* key, const char** out);
+int32_t beacon_cuda_gguf_get_array_len(const BeaconCudaGguf* f, const char* key, uint64_t* out);
+/* GgufFile::model_config (config_map.rs:14-100): fills the architecture
+ * fields of `cfg` from {arch}.embedding_length, block_count,
+ * attention.head_count(_kv), attention.key_length, feed_forward_length,
+ * vocab_size (or the tokenizer.ggml.tokens length), rope.freq_base and
+ * attention.layer_norm_rms_epsilon; max_context from context_length only
+ * when cfg->max_context is 0. Other fields are left as they are. */
+int32_t beacon_cuda_gguf_model_config(const BeaconCudaGguf* f, BeaconCudaModelConfig* cfg);
+/* Engine weight loading from a GGUF file (crates/beacon-core/src/weights.rs:
+ * 116-166 name mapping): token_embd (quantized embeddings are dequantised to
+ * f16 on the device), output_norm, output (or the tied token_embd),
+ * blk.N.{attn_norm, attn_q, attn_k, attn_v, attn_output, ffn_norm, ffn_gate,
+ * ffn_up, ffn_down}. Q4_0 bytes are read in the GGUF split nibble order. A
+ * missing tensor is INVALID_ARGUMENT (EngineError::WeightNotFound), a shape
+ * that disagrees with the model SHAPE_MISMATCH, bias tensors
+ * UNSUPPORTED_DTYPE. */
+int32_t beacon_cuda_model_load_gguf(BeaconCudaModel* model, const BeaconCudaGguf* f);
+
 /* === Tensor parallelism (NCCL over NVLink) === */
 /* 128-byte ncclUniqueId, made on rank 0 and shared by the caller. */
 int32_t beacon_cuda_comm_unique_id(void* out_id_128);
