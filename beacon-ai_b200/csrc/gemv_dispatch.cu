@@ -102,11 +102,19 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
     bool mma = mode == MODE_FAST && mma_env != 0 &&
                (mma_env == 2 || pl.bpad >= 4 || L.dtype == BEACON_CUDA_DTYPE_Q8_0);
     const size_t tb = (size_t)L.tile_bytes;
-    size_t xb = gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad);
-    // the tensor-core consumer's scratch must leave room for two ring stages;
-    // where it does not, the dp2a consumer (no scratch) keeps the plan
-    if (mma && xb + gemv3_mma_bytes(L.dtype, pl.bpad) + 256 + 2 * kG3Warps * tb > budget) mma = false;
-    if (mma) xb += gemv3_mma_bytes(L.dtype, pl.bpad);
+    auto x_bytes = [&](bool use_mma) {
+        return gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad) +
+               (use_mma ? gemv3_mma_bytes(L.dtype, pl.bpad) : 0);
+    };
+    auto ring_stages = [&](bool use_mma) {
+        const size_t x = x_bytes(use_mma);
+        return x + 256 + 2 * kG3Warps * tb > budget ? 0 : (int)std::min<size_t>(6, (budget - x - 256) / (kG3Warps * tb));
+    };
+    // The tensor-core consumer's scratch must leave room for two ring stages
+    // (three for Q8_0, whose slot is refilled only after its MMAs read it);
+    // where it does not, the dp2a consumer (no scratch) keeps the plan.
+    if (mma && ring_stages(true) < (L.dtype == BEACON_CUDA_DTYPE_Q8_0 ? 3 : 2)) mma = false;
+    const size_t xb = x_bytes(mma);
     if (xb + 256 + 2 * kG3Warps * tb > budget) return pl;
     int stages = (int)std::min<size_t>(6, (budget - xb - 256) / (kG3Warps * tb));
     const bool pairable = pl.bpad <= 2 && xb + 256 + 2 * kG3Warps * tb <= half_sm;
@@ -150,16 +158,16 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
 }
 
 // Rows of the next launch out of `rem` (1..16): the persistent kernel takes
-// up to 8 rows at a time; 9..16 rows go in 8-row launches when an 8-row plan
-// fits (each reads the weights again, still far faster than one 16-row launch
-// of the tiled kernel), else in one tiled launch; up to 8 rows whose
-// persistent plan does not fit shared memory (staged activations of a long K)
-// go in 4-, 2- or 1-row launches, else in one tiled launch.
+// up to 8 rows at a time, in the largest of 8-, 4-, 2- or 1-row launches
+// whose plan fits shared memory (staged activations of a long K); each reads
+// the weights again, still faster than one launch of the tiled kernel (which
+// is issue-bound at many rows: 1.3 ms against 0.23 ms for a 16-row 128256 x
+// 4096 Q4_0 GEMV, measured). Only when no persistent plan fits at all does
+// the tiled kernel take them all.
 int linear_chunk_rows(const BeaconCudaContext* ctx, const QLayout& L, int rem, int mode) {
     const int b = std::min(16, rem);
-    if (b > 8) return plan_linear(ctx, L, 8, mode).v3 ? 8 : b;  // 8-row persistent launches, else one tiled
-    if (plan_linear(ctx, L, b, mode).v3) return b;
-    for (int c : {4, 2, 1})
+    if (b <= 8 && plan_linear(ctx, L, b, mode).v3) return b;
+    for (int c : {8, 4, 2, 1})
         if (c < b && plan_linear(ctx, L, c, mode).v3) return c;
     return b;
 }

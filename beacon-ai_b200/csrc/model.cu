@@ -36,6 +36,7 @@ namespace bc {
 namespace {
 
 constexpr int kPrefillChunk = 2048;
+constexpr int kDecodeGemvRows = 64;  // decode steps up to this many sequences keep the GEMV
 
 // --- small kernels ------------------------------------------------------------
 
@@ -197,6 +198,11 @@ struct BeaconCudaModel {
     size_t attn_cnt_count = 0;
     std::unique_ptr<bc::DeviceBuffer> argmax_buf;
     bool pdl = true;  // programmatic dependent launch between the step's kernels
+    // rows above which a fast-numerics linear runs as the tensor-core GEMM
+    // (prefill: 16; a decode step of up to kDecodeGemvRows sequences keeps the
+    // persistent GEMV in 8-row launches, which stream the weights at a far
+    // higher rate than the GEMM's 256-row tiles filled by a few rows)
+    int gemm_rows = 16;
     bc::ArgmaxSummary* argmax_scratch = nullptr;
     // device sampling: [work rows | argmax summaries | uniforms | previous tokens | next tokens]
     std::unique_ptr<bc::DeviceBuffer> samp_buf;
@@ -253,7 +259,7 @@ int gemv_rows(const BeaconCudaModel* m, const QLayout& L, int rem) {
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
             int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s, const QkvEpi* qkv = nullptr,
             const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
-    if (rows > 16 && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L)) {
+    if (rows > m->gemm_rows && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L)) {
         QkvEpi qe;
         if (qkv) {
             qe = *qkv;
@@ -288,7 +294,8 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
                    float* y, int64_t y_ld, int epi, cudaStream_t s, const QkvEpi* qkv = nullptr,
                    const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
     const int64_t hid = m->cfg.hidden_size;
-    bool fused = true;
+    // the tensor-core GEMM takes the rows (linear() below): normalise first
+    bool fused = !(rows > m->gemm_rows && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L));
     for (int r0 = 0, b = 0; r0 < rows && fused; r0 += b) {
         b = gemv_rows(m, L, rows - r0);
         fused = plan_linear(m->ctx, L, b, gemv_mode(m)).v3;
@@ -316,6 +323,7 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
 // one position (decode) or consecutive tokens of sequence 0 (prefill chunk).
 // pos_ptr != nullptr: positions come from device memory (graph capture).
 void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, int pos_imm, cudaStream_t s) {
+    m->gemm_rows = decode ? kDecodeGemvRows : 16;
     const auto& c = m->cfg;
     const int64_t hid = c.hidden_size;
     const int D = c.head_dim;
@@ -1120,6 +1128,8 @@ int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* m, BeaconCudaStream* s
                 default: return m->wlm->ptr;
             }
         };
+        // the kernels a decode step of `batch` sequences runs (or a prefill chunk's)
+        m->gemm_rows = batch <= kDecodeGemvRows ? kDecodeGemvRows : 16;
         auto pass = [&]() {
             for (int li = 0; li < nl; ++li)
                 linear(m, *Lp, weight(li), x, x_ld, batch, y, y_ld, epi, nullptr, 0, s);

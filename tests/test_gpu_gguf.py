@@ -66,7 +66,7 @@ def build(tmp_path, quantized_embedding: bool):
         lin(p + "ffn_down.weight", H, FFN, kinds["ffn_down"])
     for name, shape, t, data in tensors:
         b.add_tensor(name, shape, t, data)
-    return b.write(tmp_path / ("q" if quantized_embedding else "f") + ".gguf"), tensors
+    return b.write(tmp_path / ("q.gguf" if quantized_embedding else "f.gguf")), tensors
 
 
 def oracle_from(tensors, rtz):
