@@ -168,6 +168,7 @@ struct BeaconCudaModel {
     int h_loc = 0, kv_loc = 0, f_loc = 0;
     int64_t v_loc = 0, v0 = 0, qd = 0, kd = 0, qkv_n = 0;
     int32_t wdtype = -1;
+    int32_t kind_dtype[5] = {-1, -1, -1, -1, -1};  // block type of lm_head, q/k/v, o, gate/up, down
     bc::QLayout Lqkv, Lo, Lgu, Ld, Llm;
     std::vector<bc::LayerW> layers;
     std::unique_ptr<bc::DeviceBuffer> embed, final_norm, wlm, rope_cs, rope_sn;
@@ -729,11 +730,24 @@ int32_t beacon_cuda_model_set_weight(BeaconCudaModel* m, int32_t layer, int32_t 
         cudaStream_t s = m->ctx->internal;
         const bool dev = on_device != 0;
         const int64_t H = c.hidden_size, D = c.head_dim;
+        // One tile layout per projection kind serves every layer, and q/k/v
+        // (and gate/up) share one fused tile: each kind needs one block type
+        // across the model. Anything else is refused rather than misread.
         auto quant_check = [&]() {
             if (!is_quantized(dtype)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "linear weights must be GGUF blocks");
             if (m->wdtype < 0) {
                 m->wdtype = dtype;
             }
+            const int kind = slot == BEACON_CUDA_W_LM_HEAD ? 0
+                             : (slot == BEACON_CUDA_W_Q || slot == BEACON_CUDA_W_K || slot == BEACON_CUDA_W_V) ? 1
+                             : slot == BEACON_CUDA_W_O ? 2
+                             : (slot == BEACON_CUDA_W_GATE || slot == BEACON_CUDA_W_UP) ? 3 : 4;
+            if (m->kind_dtype[kind] >= 0 && m->kind_dtype[kind] != dtype)
+                fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE,
+                     "model_set_weight: block type " + std::to_string(dtype) + " after " +
+                         std::to_string(m->kind_dtype[kind]) +
+                         ": q/k/v, o, gate/up and down each need one block type across all layers");
+            m->kind_dtype[kind] = dtype;
         };
         auto identity_map = [](const QLayout& L, int64_t r0, int64_t nr, int64_t src0) {
             std::vector<int64_t> map((size_t)L.n_pad, -2);

@@ -32,7 +32,12 @@ def sane_blocks(rng, t, n, k, scale=0.001):
     return sb(rng, ORC_TYPE[t], n, k, scale)
 
 
-def build(tmp_path, quantized_embedding: bool):
+# q/k/v share one fused tile and gate/up another, so each group has one block type
+KINDS = {"attn_q": "Q4_0", "attn_k": "Q4_0", "attn_v": "Q4_0", "attn_output": "Q4_K", "ffn_gate": "Q5_K",
+         "ffn_up": "Q5_K", "ffn_down": "Q6_K"}
+
+
+def build(tmp_path, quantized_embedding: bool, kinds=None, name=None):
     rng = np.random.default_rng(7 + quantized_embedding)
     b = llama_kv(GgufBuilder(), H, LAYERS, HEADS, KV_HEADS, FFN, VOCAB)
     tensors = []   # (name, shape, type, data)
@@ -51,8 +56,7 @@ def build(tmp_path, quantized_embedding: bool):
         tensors.append(("token_embd.weight", (VOCAB, H), "F16", rng.standard_normal((VOCAB, H)).astype(np.float16)))
         lin("output.weight", VOCAB, H, "Q6_K")
     tensors.append(("output_norm.weight", (H,), "F32", (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)))
-    kinds = {"attn_q": "Q4_0", "attn_k": "Q4_0", "attn_v": "Q8_0", "attn_output": "Q4_K", "ffn_gate": "Q5_K",
-             "ffn_up": "Q4_K", "ffn_down": "Q6_K"}
+    kinds = dict(KINDS, **(kinds or {}))
     for li in range(LAYERS):
         p = f"blk.{li}."
         tensors.append((p + "attn_norm.weight", (H,), "F32", (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)))
@@ -66,7 +70,7 @@ def build(tmp_path, quantized_embedding: bool):
         lin(p + "ffn_down.weight", H, FFN, kinds["ffn_down"])
     for name, shape, t, data in tensors:
         b.add_tensor(name, shape, t, data)
-    return b.write(tmp_path / ("q.gguf" if quantized_embedding else "f.gguf")), tensors
+    return b.write(tmp_path / (name or ("q.gguf" if quantized_embedding else "f.gguf"))), tensors
 
 
 def oracle_from(tensors, rtz):
@@ -135,3 +139,17 @@ def test_load_gguf_reports_missing_and_misshapen_tensors(be, tmp_path):
     m2 = CudaModel(be, DecoderConfig(**g.model_config(max_context=16)))
     with pytest.raises(EngineError, match="blk.1.ffn_up.weight"):
         m2.load_gguf(g)
+
+
+def test_load_gguf_refuses_mixed_qkv_block_types(be, tmp_path):
+    """q/k/v share one tile layout: a file whose attn_v has another block type
+    than attn_q is refused (UNSUPPORTED_DTYPE) instead of being misread."""
+    from beacon_cuda import CudaModel, DecoderConfig, EngineError
+    from beacon_cuda import _lib as L
+    from beacon_cuda.gguf import GgufFile
+    path, _ = build(tmp_path, False, kinds={"attn_v": "Q8_0"}, name="mixed.gguf")
+    f = GgufFile(path)
+    m = CudaModel(be, DecoderConfig(**f.model_config(max_context=16)))
+    with pytest.raises(EngineError) as e:
+        m.load_gguf(f)
+    assert e.value.status == L.ERR_UNSUPPORTED_DTYPE and "blk.0.attn_v.weight" in str(e.value)
