@@ -41,6 +41,7 @@ struct Gemv3Params {
     int64_t total_warps;
     int stages;
     int kspan;            // staged activation columns (k_pad)
+    int xstride;          // int16 codes between staged rows (kspan, +8 for the tensor-core consumer)
     float* slots;         // [CTAs][2][B][32] partial sums of the CTAs' first and last groups
     int* counters;        // [groups], zero at rest
     int* err;             // set to kErrGemvWait when a wait gives up
@@ -110,7 +111,7 @@ __device__ __forceinline__ uint32_t pack_i16x2(int lo, int hi) { return (uint32_
 // covers columns (p0 + i) * 1024 + 4 * threadIdx.x.
 template <int FMT, int MODE, int NP>
 __device__ __forceinline__ void store_passes(const float4 (&v)[NP], int p0, int kspan, uint8_t* xs, int b, int B,
-                                             int nblk) {
+                                             int nblk, int xstride) {
     const int tid = threadIdx.x;
     if (MODE == MODE_F32) {
 #pragma unroll
@@ -120,8 +121,10 @@ __device__ __forceinline__ void store_passes(const float4 (&v)[NP], int p0, int 
         }
         return;
     }
-    int16_t* xq = reinterpret_cast<int16_t*>(xs) + (size_t)b * kspan;
-    float2* sxq = reinterpret_cast<float2*>(xs + (size_t)B * kspan * 2) + b * nblk;  // (scale, code sum)
+    // code rows xstride int16 apart (the tensor-core consumer pads them so
+    // that the batch rows of one column fall in different banks)
+    int16_t* xq = reinterpret_cast<int16_t*>(xs) + (size_t)b * xstride;
+    float2* sxq = reinterpret_cast<float2*>(xs + (size_t)B * xstride * 2) + b * nblk;  // (scale, code sum)
     float am[NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i) am[i] = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
@@ -170,7 +173,7 @@ __device__ __forceinline__ void store_passes(const float4 (&v)[NP], int p0, int 
 // size), normalised with inv and the norm weights when given, then stored.
 template <int FMT, int MODE, int NP>
 __device__ __forceinline__ void stage_chunk(const GemvParams& p, bool vec, bool wvec, int b, int p0, float inv,
-                                            int kspan, uint8_t* xs, int B, int nblk) {
+                                            int kspan, uint8_t* xs, int B, int nblk, int xstride) {
     float4 v[NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i) v[i] = load_x4(p, vec, b, (int64_t)((p0 + i) * 256 + threadIdx.x) * 4);
@@ -184,14 +187,14 @@ __device__ __forceinline__ void stage_chunk(const GemvParams& p, bool vec, bool 
             v[i].w = v[i].w * inv * w.w;
         }
     }
-    store_passes<FMT, MODE, NP>(v, p0, kspan, xs, b, B, nblk);
+    store_passes<FMT, MODE, NP>(v, p0, kspan, xs, b, B, nblk, xstride);
 }
 
 // Register-held rows (passes <= 8): NP = passes rounded up to a power of two.
 template <int FMT, int MODE, int NP>
 __device__ __forceinline__ void stage_held(const GemvParams& p, const float4 (&xr)[kStageRegPasses],
                                            const float4 (&nwr)[kStageRegPasses], float inv, int kspan, uint8_t* xs,
-                                           int b, int B, int nblk) {
+                                           int b, int B, int nblk, int xstride) {
     float4 v[NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
@@ -203,14 +206,14 @@ __device__ __forceinline__ void stage_held(const GemvParams& p, const float4 (&x
             v[i].w = v[i].w * inv * nwr[i].w;
         }
     }
-    store_passes<FMT, MODE, NP>(v, 0, kspan, xs, b, B, nblk);
+    store_passes<FMT, MODE, NP>(v, 0, kspan, xs, b, B, nblk, xstride);
 }
 
 // Staging of all K columns (FAST: int16 codes + scale + code sum per 32;
 // F32: floats), rows b >= batch and columns >= k as zeros, with the optional
 // RMSNorm (x * inv_rms) * w of ops.rs:77-93. All threads of the CTA take part.
 template <int FMT, int MODE, int B>
-__device__ __forceinline__ void stage_x_full(const GemvParams& p, uint8_t* xs, int kspan,
+__device__ __forceinline__ void stage_x_full(const GemvParams& p, uint8_t* xs, int kspan, int xstride,
                                              const float4 (&nwr)[kStageRegPasses]) {
     __shared__ float part[B][kG3Warps];
     constexpr int R = kStageRegPasses;
@@ -269,25 +272,25 @@ __device__ __forceinline__ void stage_x_full(const GemvParams& p, uint8_t* xs, i
         }
         if (held) {
             if (passes <= 1)
-                stage_held<FMT, MODE, 1>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+                stage_held<FMT, MODE, 1>(p, xr, nwr, inv, kspan, xs, b, B, nblk, xstride);
             else if (passes <= 2)
-                stage_held<FMT, MODE, 2>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+                stage_held<FMT, MODE, 2>(p, xr, nwr, inv, kspan, xs, b, B, nblk, xstride);
             else if (passes <= 4)
-                stage_held<FMT, MODE, 4>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+                stage_held<FMT, MODE, 4>(p, xr, nwr, inv, kspan, xs, b, B, nblk, xstride);
             else
-                stage_held<FMT, MODE, 8>(p, xr, nwr, inv, kspan, xs, b, B, nblk);
+                stage_held<FMT, MODE, 8>(p, xr, nwr, inv, kspan, xs, b, B, nblk, xstride);
         } else {
             int p0 = 0;
-            for (; p0 + 8 <= passes; p0 += 8) stage_chunk<FMT, MODE, 8>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+            for (; p0 + 8 <= passes; p0 += 8) stage_chunk<FMT, MODE, 8>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk, xstride);
             if (p0 + 4 <= passes) {
-                stage_chunk<FMT, MODE, 4>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+                stage_chunk<FMT, MODE, 4>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk, xstride);
                 p0 += 4;
             }
             if (p0 + 2 <= passes) {
-                stage_chunk<FMT, MODE, 2>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+                stage_chunk<FMT, MODE, 2>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk, xstride);
                 p0 += 2;
             }
-            if (p0 < passes) stage_chunk<FMT, MODE, 1>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk);
+            if (p0 < passes) stage_chunk<FMT, MODE, 1>(p, vec, wvec, b, p0, inv, kspan, xs, B, nblk, xstride);
         }
     }
 }
@@ -320,8 +323,8 @@ __device__ __forceinline__ void g3_consume_tile(const G3Tile<FMT>& r, const uint
 // Bytes of the staged activations (FAST: int16 codes, then per 32-column
 // block a float scale and an int code sum; F32: floats), 16-byte multiple.
 template <int MODE, int B>
-__host__ __device__ __forceinline__ size_t g3_x_bytes(int kspan) {
-    return MODE == MODE_F32 ? (size_t)B * kspan * 4 : (size_t)B * kspan * 2 + (size_t)B * (kspan / 32) * 8;
+__host__ __device__ __forceinline__ size_t g3_x_bytes(int kspan, int xstride) {
+    return MODE == MODE_F32 ? (size_t)B * kspan * 4 : (size_t)B * xstride * 2 + (size_t)B * (kspan / 32) * 8;
 }
 inline size_t gemv3_red_bytes(int bpad) { return (size_t)kG3Warps * 2 * bpad * 32 * 4; }
 
@@ -356,9 +359,8 @@ __device__ __forceinline__ G3Range g3_range(uint32_t T) {
 // stores. Whole warp. The sum is scaled by inv (1/rms rows) before the
 // epilogue. red: [8 warps][2][B][32] floats; cnt: the CTA's arrival counters.
 template <int B>
-__device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t KT,
-                                                int lane, float (&acc)[B],
-                                                const float (&inv)[B], float* red, int* cnt,
+__device__ __forceinline__ void g3_finish_group(const Gemv3Params& a, int epi, uint32_t g, uint32_t KT, int lane,
+                                                float (&acc)[B], const float (&inv)[B], float* red, int* cnt,
                                                 const EpiPre<B>& pre) {
     const GemvParams& p = a.p;
     const G3Range r = g3_range((uint32_t)a.total_tiles);
@@ -455,7 +457,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                       // [warps][S]
     uint8_t* ring = smem + 128 * ((kG3Warps * S * 8 + 127) / 128);           // [warps][S][tile]
     uint8_t* xs = ring + (size_t)kG3Warps * S * tb;                          // staged activations
-    float* red = reinterpret_cast<float*>(xs + g3_x_bytes<MODE, B>(a.kspan));  // [warps][2][B][32] partials
+    float* red = reinterpret_cast<float*>(xs + g3_x_bytes<MODE, B>(a.kspan, a.xstride));  // [warps][2][B][32] partials
     uint64_t* mybar = bars + warp * S;
     uint8_t* myring = ring + (size_t)warp * S * tb;
 
@@ -511,11 +513,18 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     if (from_image) {
         // the producer's staging image: bulk copies, and 1/rms from its block sums
         __syncthreads();
-        const uint32_t bytes = (uint32_t)B * a.kspan * 2 + (uint32_t)B * (a.kspan / 32) * 8;  // the FAST image
+        // the FAST image: B rows of kspan codes, then the block scales; rows
+        // land xstride codes apart
+        const uint32_t row_bytes = (uint32_t)a.kspan * 2, sc_bytes = (uint32_t)B * (a.kspan / 32) * 8;
         if (threadIdx.x == 0) {
-            mbar_expect_tx(&qx_bar, bytes);
-            for (uint32_t off = 0; off < bytes; off += 16384u)
-                bulk_g2s(xs + off, p.qx.data + off, min(16384u, bytes - off), &qx_bar);
+            mbar_expect_tx(&qx_bar, (uint32_t)B * row_bytes + sc_bytes);
+            for (int b = 0; b < B; ++b)
+                for (uint32_t off = 0; off < row_bytes; off += 16384u)
+                    bulk_g2s(xs + (size_t)b * a.xstride * 2 + off, p.qx.data + (size_t)b * row_bytes + off,
+                             min(16384u, row_bytes - off), &qx_bar);
+            for (uint32_t off = 0; off < sc_bytes; off += 16384u)
+                bulk_g2s(xs + (size_t)B * a.xstride * 2 + off, p.qx.data + (size_t)B * row_bytes + off,
+                         min(16384u, sc_bytes - off), &qx_bar);
         }
         // warp b sums row b's block sums of squares (B <= 8 warps)
         if (p.qx.ss && warp < B) {
@@ -532,7 +541,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             }
         }
     } else {
-        stage_x_full<FMT, MODE, B>(p, xs, a.kspan, nwr);
+        stage_x_full<FMT, MODE, B>(p, xs, a.kspan, a.xstride, nwr);
     }
     __syncthreads();
     if (from_image && p.qx.ss) {
@@ -574,7 +583,7 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
             mma_scales<FMT>(tp, lane, scr);
             __syncwarp();
             if (FMT != FMT_Q8_0) refill();  // Q4 tiles are in registers now
-            mma_consume_tile<FMT, B>(regs, tp, xs, a.kspan, (int)t, scr, macc, lane);
+            mma_consume_tile<FMT, B>(regs, tp, xs, a.kspan, a.xstride, (int)t, scr, macc, lane);
             if (FMT == FMT_Q8_0) {
                 __syncwarp();
                 refill();
@@ -607,8 +616,13 @@ __global__ void __launch_bounds__(kG3Warps * 32, (B <= 2 ? 2 : 1)) qgemv3_kernel
     }
 }
 
-inline size_t gemv3_x_bytes(int mode, int bpad, int64_t kspan) {
-    return mode == MODE_F32 ? (size_t)bpad * kspan * 4 : (size_t)bpad * kspan * 2 + (size_t)bpad * (kspan / 32) * 8;
+// Staged row stride in int16 codes: the tensor-core consumer reads one column
+// block of all B rows together, so its rows are padded by 16 bytes to fall in
+// different shared-memory banks.
+inline int64_t gemv3_xstride(bool mma, int64_t kspan) { return mma ? kspan + 8 : kspan; }
+inline size_t gemv3_x_bytes(int mode, int bpad, int64_t kspan, bool mma = false) {
+    return mode == MODE_F32 ? (size_t)bpad * kspan * 4
+                            : (size_t)bpad * gemv3_xstride(mma, kspan) * 2 + (size_t)bpad * (kspan / 32) * 8;
 }
 inline size_t gemv3_bar_bytes(int stages) { return 128 * (((size_t)kG3Warps * stages * 8 + 127) / 128); }
 // Per-CTA scratch of the tensor-core consumer (block scales / row transpose).
@@ -650,6 +664,7 @@ void launch_qgemv3_t(const LinearPlan& pl, const GemvLaunch& a) {
     q.total_warps = pl.total_warps;
     q.stages = pl.stages;
     q.kspan = (int)a.L->k_pad;
+    q.xstride = (int)gemv3_xstride(MMA, a.L->k_pad);
     q.slots = a.scratch.partial;
     q.counters = a.scratch.counters;
     q.err = a.scratch.err;

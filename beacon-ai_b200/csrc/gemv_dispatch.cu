@@ -103,7 +103,7 @@ LinearPlan plan_linear(const BeaconCudaContext* ctx, const QLayout& L, int batch
                (mma_env == 2 || pl.bpad >= 4 || L.dtype == BEACON_CUDA_DTYPE_Q8_0);
     const size_t tb = (size_t)L.tile_bytes;
     auto x_bytes = [&](bool use_mma) {
-        return gemv3_x_bytes(mode, pl.bpad, L.k_pad) + gemv3_red_bytes(pl.bpad) +
+        return gemv3_x_bytes(mode, pl.bpad, L.k_pad, use_mma) + gemv3_red_bytes(pl.bpad) +
                (use_mma ? gemv3_mma_bytes(L.dtype, pl.bpad) : 0);
     };
     auto ring_stages = [&](bool use_mma) {

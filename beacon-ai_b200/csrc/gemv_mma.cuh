@@ -157,11 +157,13 @@ struct MmaAcc {
     float v[4][2];
 };
 
-// Consume one tile. xs: the staged activation image (int16 codes [B][kspan],
-// then (scale, code sum) float2 [B][kspan/32]); tile: the k-tile index.
+// Consume one tile. xs: the staged activation image (int16 codes of B rows
+// xstride apart, then (scale, code sum) float2 [B][kspan/32]); tile: the
+// k-tile index.
 template <int FMT, int B>
 __device__ __forceinline__ void mma_consume_tile(const MmaTileRegs<FMT>& r, const uint8_t* tp, const uint8_t* xs,
-                                                 int kspan, int tile, const float* scr, MmaAcc& acc, int lane) {
+                                                 int kspan, int xstride, int tile, const float* scr, MmaAcc& acc,
+                                                 int lane) {
     static_assert(B == 1 || B == 2 || B == 4 || B == 8, "batch rows per MMA column set");
     constexpr int NB = B, SB = 8 / B;
     constexpr bool AS = FMT == FMT_Q8_0;
@@ -169,13 +171,13 @@ __device__ __forceinline__ void mma_consume_tile(const MmaTileRegs<FMT>& r, cons
     const int jj_g = g / NB, b_g = g % NB;  // the block-in-set and batch row this thread's column stands for
     const int16_t* xq = reinterpret_cast<const int16_t*>(xs);
     const int nblk = kspan / 32;
-    const float2* sx = reinterpret_cast<const float2*>(xs + (size_t)B * kspan * 2);
+    const float2* sx = reinterpret_cast<const float2*>(xs + (size_t)B * xstride * 2);
     const int zero[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int s = 0; s < NB; ++s) {
         // activation codes of this thread's block of the set, split into bytes
         const int blk_g = tile * 8 + s * SB + jj_g;
-        const int16_t* src = xq + (size_t)b_g * kspan + blk_g * 32;
+        const int16_t* src = xq + (size_t)b_g * xstride + blk_g * 32;
         uint32_t h0, h1, l0, l1;
         if (FMT == FMT_Q4_0) {
             const uint4 v = *reinterpret_cast<const uint4*>(src + 8 * t);
