@@ -281,8 +281,9 @@ __global__ void decode_attn_combine_kernel(const DecodeAttnArgs a, int d) {
 // semantics: max-subtracted exp, normalised at the end) reduces over the 8
 // threads of a pair group with shuffles; the same thread then owns those
 // pairs' outputs for dims (t%8) D/8 .. +D/8, so the rescale stays local.
-// f32 arithmetic; used for prefill in the fast numerics (the row kernel above
-// keeps the reference's summation order for the exact ones).
+// f32 arithmetic; used for prefill in the fast numerics over f32 caches (f16
+// caches take the tensor-core kernel below; the row kernel above keeps the
+// reference's summation order for the exact numerics).
 constexpr int kPfKeys = 64;
 constexpr int kPfPairs = 128;
 constexpr int kPfThreads = 256;
@@ -443,10 +444,217 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const AttnR
     }
 }
 
+// Prefill attention on the tensor cores (fast numerics, f16 caches) ----------------
+// Same work split as prefill_attn_kernel: one CTA (8 warps) per (128/G query
+// rows, KV head); warp w owns the 16 (row, head) pairs 16w .. 16w+15 (pair =
+// row * G + head) as the M dimension of m16n8k16 f16 MMAs with f32
+// accumulation. Key/value tiles of 64 keys are double-buffered in shared
+// memory by 16-byte asynchronous copies at swizzled positions (chunk ^ (row &
+// 7), conflict-free ldmatrix). Scores S = Q K^T with the pre-scaled query in
+// registers as f16 high and low parts (two MMAs, ~22-bit query precision);
+// online softmax on the accumulator fragments (row max and sum over the 4
+// lanes of a row); P rounded to f16 is re-packed in registers as the A
+// operand of O += P V, V^T fragments from transposing ldmatrix. The causal CTAs
+// are launched heaviest (latest query rows) first.
+constexpr int kPtKeys = 64;
+
+template <int D>
+struct PtLayout {
+    static constexpr int row = 2 * D;                 // bytes of one key or value row
+    static constexpr int stage = 2 * kPtKeys * row;   // keys, then values
+    static constexpr size_t smem = 2 * (size_t)stage;  // two stages
+};
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(const AttnRowsArgs a) {
+    using Lay = PtLayout<D>;
+    constexpr int RT = kPfPairs / G;  // query rows per CTA
+    constexpr int KS = D / 16;        // 16-dim k-steps of the scores
+    constexpr int NT = kPtKeys / 8;   // 8-key n-tiles of the scores
+    constexpr int ND = D / 8;         // 8-dim n-tiles of the output
+    constexpr int CPR = D / 8;        // 16-byte chunks per row
+    extern __shared__ __align__(128) uint8_t pt_smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int kvh = blockIdx.y;
+    const int64_t r0 = (int64_t)(gridDim.x - 1 - blockIdx.x) * RT;  // heaviest tiles first
+    // the two pairs of this thread's fragment rows
+    const int pa = warp * 16 + g, pb = pa + 8;
+    const int64_t row_a = r0 + pa / G, row_b = r0 + pb / G;
+    const int ha = kvh * G + pa % G, hb = kvh * G + pb % G;
+    // query fragments (A operand, 16 pairs x 16 dims per k-step), pre-scaled,
+    // as f16 high and low parts: regs (pair a, dims 2t..), (pair b, 2t..),
+    // (pair a, 8 + 2t..), (pair b, 8 + 2t..)
+    uint32_t qh[KS][4], ql[KS][4];
+    {
+        const float* q = reinterpret_cast<const float*>(a.q);
+#pragma unroll
+        for (int j = 0; j < KS; ++j)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const bool second = r & 1;
+                const int64_t row = second ? row_b : row_a;
+                const int h = second ? hb : ha;
+                const int d = 16 * j + 2 * t + (r >> 1) * 8;
+                float x0 = 0.0f, x1 = 0.0f;
+                if (row < a.sq) {
+                    const float* qp = q + h * a.q_sh + row * a.q_ss + d;
+                    x0 = qp[0] * a.scale;
+                    x1 = qp[1] * a.scale;
+                }
+                const __half2 hh = __floats2half2_rn(x0, x1);
+                const float2 hf = __half22float2(hh);
+                qh[j][r] = *reinterpret_cast<const uint32_t*>(&hh);
+                ql[j][r] = pack_f16x2(x0 - hf.x, x1 - hf.y);
+            }
+    }
+    // keys [0, skv); causal: row s sees keys <= skv - sq + s
+    const int64_t last_row = min((int64_t)a.sq - 1, r0 + RT - 1);
+    const int64_t kend = a.causal ? min((int64_t)a.skv, a.skv - a.sq + last_row + 1) : (int64_t)a.skv;
+    const int64_t lim_a = a.causal ? (int64_t)a.skv - a.sq + row_a : (int64_t)a.skv - 1;
+    const int64_t lim_b = a.causal ? (int64_t)a.skv - a.sq + row_b : (int64_t)a.skv - 1;
+    const __half* kc = reinterpret_cast<const __half*>(a.k) + (int64_t)kvh * a.kv_sh;
+    const __half* vc = reinterpret_cast<const __half*>(a.v) + (int64_t)kvh * a.kv_sh;
+    const int ntiles = (int)((kend + kPtKeys - 1) / kPtKeys);
+    auto issue = [&](int it) {
+        uint8_t* base = pt_smem + (size_t)(it & 1) * Lay::stage;
+        const int64_t k0 = (int64_t)it * kPtKeys;
+        for (int c = tid; c < 2 * kPtKeys * CPR; c += kPfThreads) {
+            const int rw = c / CPR, part = c - rw * CPR;
+            const int r = rw & (kPtKeys - 1);
+            const int64_t key = k0 + r;
+            uint8_t* dst = base + (rw < kPtKeys ? 0 : kPtKeys * Lay::row) + tc_swz(r, part, Lay::row);
+            if (key < kend)
+                cp_async16(dst, (rw < kPtKeys ? kc : vc) + key * a.kv_ss + part * 8);
+            else
+                *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);  // past the keys: finite zeros
+        }
+        cp_async_commit();
+    };
+    float o[ND][4];
+#pragma unroll
+    for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+    const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: the matrix this lane addresses, its row
+    if (ntiles > 0) issue(0);
+    for (int it = 0; it < ntiles; ++it) {
+        if (it + 1 < ntiles) {
+            issue(it + 1);
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
+        }
+        __syncthreads();  // every thread's copies of tile it have landed
+        const uint32_t kb = smem_u32(pt_smem + (size_t)(it & 1) * Lay::stage);
+        const uint32_t vb = kb + kPtKeys * Lay::row;
+        const int64_t k0 = (int64_t)it * kPtKeys;
+        // scores: s[n] = pairs (a, b) x keys k0 + 8n + 2t, +1
+        float sc[NT][4];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < KS; j += 2) {
+                uint32_t b0, b1, b2, b3;  // k-step j: (b0, b1); k-step j + 1: (b2, b3)
+                ldsm_x4(kb + tc_swz(8 * n + rr, 2 * j + mi, Lay::row), b0, b1, b2, b3);
+                mma_f16(sc[n], qh[j][0], qh[j][1], qh[j][2], qh[j][3], b0, b1);
+                mma_f16(sc[n], ql[j][0], ql[j][1], ql[j][2], ql[j][3], b0, b1);
+                mma_f16(sc[n], qh[j + 1][0], qh[j + 1][1], qh[j + 1][2], qh[j + 1][3], b2, b3);
+                mma_f16(sc[n], ql[j + 1][0], ql[j + 1][1], ql[j + 1][2], ql[j + 1][3], b2, b3);
+            }
+        }
+        // mask and online softmax (rows a: sc[.][0..1], b: sc[.][2..3])
+        float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int64_t key = k0 + 8 * n + 2 * t + e;
+                if (key > lim_a || key >= kend) sc[n][e] = -INFINITY;
+                if (key > lim_b || key >= kend) sc[n][2 + e] = -INFINITY;
+                mx_a = fmaxf(mx_a, sc[n][e]);
+                mx_b = fmaxf(mx_b, sc[n][2 + e]);
+            }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        const float c_a = m_a == -INFINITY ? 0.0f : expf(m_a - mn_a);
+        const float c_b = m_b == -INFINITY ? 0.0f : expf(m_b - mn_b);
+        float su_a = 0.0f, su_b = 0.0f;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                sc[n][e] = sc[n][e] == -INFINITY ? 0.0f : expf(sc[n][e] - mn_a);
+                sc[n][2 + e] = sc[n][2 + e] == -INFINITY ? 0.0f : expf(sc[n][2 + e] - mn_b);
+                su_a += sc[n][e];
+                su_b += sc[n][2 + e];
+            }
+        su_a += __shfl_xor_sync(0xffffffffu, su_a, 1);
+        su_a += __shfl_xor_sync(0xffffffffu, su_a, 2);
+        su_b += __shfl_xor_sync(0xffffffffu, su_b, 1);
+        su_b += __shfl_xor_sync(0xffffffffu, su_b, 2);
+        l_a = l_a * c_a + su_a;
+        l_b = l_b * c_b + su_b;
+        m_a = mn_a;
+        m_b = mn_b;
+#pragma unroll
+        for (int n = 0; n < ND; ++n) {
+            o[n][0] *= c_a;
+            o[n][1] *= c_a;
+            o[n][2] *= c_b;
+            o[n][3] *= c_b;
+        }
+        // O += P V: P (16 pairs x 16 keys per k-step) from the score fragments
+#pragma unroll
+        for (int kk = 0; kk < kPtKeys / 16; ++kk) {
+            const uint32_t p0 = pack_f16x2(sc[2 * kk][0], sc[2 * kk][1]);
+            const uint32_t p1 = pack_f16x2(sc[2 * kk][2], sc[2 * kk][3]);
+            const uint32_t p2 = pack_f16x2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+            const uint32_t p3 = pack_f16x2(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+            for (int n = 0; n < ND; n += 2) {
+                uint32_t b0, b1, b2, b3;  // dims 8n..: (b0, b1); dims 8(n+1)..: (b2, b3)
+                ldsm_x4_t(vb + tc_swz(16 * kk + (mi & 1) * 8 + rr, n + (mi >> 1), Lay::row), b0, b1, b2, b3);
+                mma_f16(o[n], p0, p1, p2, p3, b0, b1);
+                mma_f16(o[n + 1], p0, p1, p2, p3, b2, b3);
+            }
+        }
+        __syncthreads();  // every warp is done with this stage before it is refilled
+    }
+    const float inv_a = l_a > 0.0f ? 1.0f / l_a : 0.0f, inv_b = l_b > 0.0f ? 1.0f / l_b : 0.0f;
+#pragma unroll
+    for (int n = 0; n < ND; ++n) {
+        const int d = 8 * n + 2 * t;
+        if (row_a < a.sq)
+            *reinterpret_cast<float2*>(a.out + ha * a.o_sh + row_a * a.o_ss + d) =
+                make_float2(o[n][0] * inv_a, o[n][1] * inv_a);
+        if (row_b < a.sq)
+            *reinterpret_cast<float2*>(a.out + hb * a.o_sh + row_b * a.o_ss + d) =
+                make_float2(o[n][2] * inv_b, o[n][3] * inv_b);
+    }
+}
+
 template <int D, int G>
 void launch_prefill_t(const AttnRowsArgs& a, cudaStream_t s) {
     constexpr int RT = kPfPairs / G;
     dim3 grid((unsigned)((a.sq + RT - 1) / RT), (unsigned)a.kv_heads);
+    if (a.kv_f16 && a.kv_ss % 8 == 0 && a.kv_sh % 8 == 0 && a.q_ss % 2 == 0 && a.q_sh % 2 == 0 &&
+        a.o_ss % 2 == 0 && a.o_sh % 2 == 0) {  // 16-byte cache rows, paired q / out elements
+        BC_CUDA(cudaFuncSetAttribute(prefill_attn_tc_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)PtLayout<D>::smem));
+        prefill_attn_tc_kernel<D, G><<<grid, kPfThreads, PtLayout<D>::smem, s>>>(a);
+        BC_LAUNCHED("prefill_attn_tc_kernel");
+        return;
+    }
     if (a.kv_f16) {
         allow_max_dynamic_smem(prefill_attn_kernel<D, G, __half>);
         prefill_attn_kernel<D, G, __half><<<grid, kPfThreads, PfLayout<D>::bytes, s>>>(a);

@@ -275,3 +275,23 @@ def test_fast_prefill_long_prompt_tiled_attention(be, causal):
     ref = om.forward(prompt, 0)
     got = m.forward(prompt, 0)
     assert np.abs(got - ref).max() <= LOGITS_TOL
+
+
+@pytest.mark.parametrize("head_dim,heads,kv_heads", [(128, 4, 1), (64, 8, 4), (128, 8, 1), (64, 8, 8)])
+def test_fast_prefill_tensor_core_attention_in_two_chunks(be, head_dim, heads, kv_heads):
+    """The tensor-core prefill attention (f16 MMAs, query split into f16 high
+    and low parts) over a 600-token prompt prefilled in two chunks, so the
+    second chunk's queries see 300 cached keys before their own (skv > sq),
+    for group sizes 4, 2, 8 and 1; logits of both chunks within the bar of the
+    oracle's f32 softmax."""
+    from beacon_cuda import _lib as L
+    c = small_cfg(num_layers=2, hidden_size=heads * head_dim, num_heads=heads, num_kv_heads=kv_heads,
+                  head_dim=head_dim, max_context=640)
+    w = make_weights(oracle_cfg(c), orc.Q4_K, seed=90 + head_dim + kv_heads)
+    om = build_oracle_model(oracle_cfg(c), w)
+    m = cuda_model(be, c, w, numerics=L.NUMERICS_FAST, kv_dtype=L.DTYPE_F16)
+    prompt = list(np.random.default_rng(91).integers(0, c["vocab_size"], 600))
+    for lo, hi in ((0, 300), (300, 600)):
+        ref = om.forward(prompt[lo:hi], lo)
+        got = m.forward(prompt[lo:hi], lo)
+        assert np.abs(got - ref).max() <= LOGITS_TOL, (lo, np.abs(got - ref).max())
