@@ -186,6 +186,7 @@ struct BeaconCudaModel {
     bc::GemvScratch gsc;
     std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
     std::unique_ptr<bc::DeviceBuffer> x16;  // f16 activations of the prefill GEMM
+    std::unique_ptr<bc::DeviceBuffer> w16;  // f16 weights of one layer linear (dequantise-first GEMM)
     // decode hand-off of quantised activations between kernels (one GPU, fast
     // numerics, batch <= 8): the hidden-state image (q/k/v, gate/up, lm_head
     // inputs, with per-block sums of squares for their RMSNorm) and the
@@ -255,6 +256,29 @@ int gemv_rows(const BeaconCudaModel* m, const QLayout& L, int rem) {
     return linear_chunk_rows(m->ctx, L, rem, gemv_mode(m));
 }
 
+// From this many rows a layer linear's tensor-core GEMM dequantises the
+// weights once into f16 rows and loads them by TMA (the fused dequantisation
+// would be repeated by every 256-row tile: 8 times at 2048 rows).
+constexpr int kDequantFirstRows = 1024;
+
+// The f16 weight scratch of the dequantise-first GEMM, sized for the largest
+// layer linear and allocated at its first use outside stream capture; NULL
+// while capturing (the fused form runs then).
+void* dequant_first_scratch(BeaconCudaModel* m, const QLayout& L, cudaStream_t s) {
+    if (&L == &m->Llm) return nullptr;  // vocab-sized: not worth the memory
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    BC_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (!m->w16) {
+        if (cs != cudaStreamCaptureStatusNone) return nullptr;
+        size_t bytes = 0;
+        for (const QLayout* l : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Ld})
+            if (qgemm_tc_supported(*l)) bytes = std::max(bytes, qgemm_tc_weight_scratch_bytes(*l));
+        if (bytes == 0) return nullptr;
+        m->w16 = std::make_unique<DeviceBuffer>(bytes);
+    }
+    return m->w16->bytes >= qgemm_tc_weight_scratch_bytes(L) ? m->w16->ptr : nullptr;
+}
+
 // qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.
 // More than 16 rows in the fast numerics run as one tensor-core GEMM.
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
@@ -267,7 +291,7 @@ void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x,
             qe.row0 = 0;
         }
         launch_qgemm_tc(L, w, x, false, x_ld, rows, y, y_ld, epi, res, res_ld, false, m->err_dev, s, m->x16->ptr,
-                        qkv ? &qe : nullptr);
+                        qkv ? &qe : nullptr, rows >= kDequantFirstRows ? dequant_first_scratch(m, L, s) : nullptr);
         return;
     }
     for (int r0 = 0, b = 0; r0 < rows; r0 += b) {

@@ -319,8 +319,12 @@ __device__ __forceinline__ void tc_epilogue32(const TcParams& p, int64_t m, int6
     }
 }
 
-template <int FMT>
-__global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap xmap) {
+// PRE: the weights were dequantised to f16 rows beforehand (wmap); the TMA
+// thread brings both operands' slices in and the producer warps only run the
+// epilogue.
+template <int FMT, bool PRE>
+__global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap xmap,
+                                                                  const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ uint8_t tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kTcStages], aload_bar[kTcStages], empty_bar[kTcStages], done_bar;
     __shared__ uint32_t tmem_base_s;
@@ -354,36 +358,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
     const uint32_t tmem = tmem_base_s;
 
     if (warp < kTcProducerWarps) {
-        // weight producers: half tid % 2 of W row n0 + tid / 2 of every slice
-        const int brow = tid >> 1, bh = tid & 1;
-        const int64_t wrow = n0 + brow;
-        const bool live = wrow < p.n_pad;
-        const bool rtz = p.rtz != 0;
-        RawSlice cur{}, nxt{};
-        if (live && nkb > 0) load_slice<FMT>(p, wrow, 0, bh, cur);
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % kTcStages;
-            if (live && kb + 1 < nkb) load_slice<FMT>(p, wrow, kb + 1, bh, nxt);  // in flight while this slice converts
-            if (kb >= kTcStages && !mbar_wait_bounded(&empty_bar[s], (uint32_t)((kb / kTcStages - 1) & 1))) {
-                atomicExch(p.err, kErrGemmWait);
-                failed_s = 1;
-                break;
-            }
-            uint8_t* b_s = ring + (size_t)s * kTcStage + kTcATile;
-            uint4 bv[4];
-            int bp[4] = {4 * bh, 4 * bh + 1, 4 * bh + 2, 4 * bh + 3};
-            if (live) {
-                dequant_half<FMT>(cur, kb, bh, rtz, bv, bp);
-            } else {
+        // weight producers (PRE: idle until the epilogue): half tid % 2 of W
+        // row n0 + tid / 2 of every slice
+        if constexpr (!PRE) {
+            const int brow = tid >> 1, bh = tid & 1;
+            const int64_t wrow = n0 + brow;
+            const bool live = wrow < p.n_pad;
+            const bool rtz = p.rtz != 0;
+            RawSlice cur{}, nxt{};
+            if (live && nkb > 0) load_slice<FMT>(p, wrow, 0, bh, cur);
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % kTcStages;
+                if (live && kb + 1 < nkb) load_slice<FMT>(p, wrow, kb + 1, bh, nxt);  // in flight while this slice converts
+                if (kb >= kTcStages && !mbar_wait_bounded(&empty_bar[s], (uint32_t)((kb / kTcStages - 1) & 1))) {
+                    atomicExch(p.err, kErrGemmWait);
+                    failed_s = 1;
+                    break;
+                }
+                uint8_t* b_s = ring + (size_t)s * kTcStage + kTcATile;
+                uint4 bv[4];
+                int bp[4] = {4 * bh, 4 * bh + 1, 4 * bh + 2, 4 * bh + 3};
+                if (live) {
+                    dequant_half<FMT>(cur, kb, bh, rtz, bv, bp);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) bv[i] = make_uint4(0, 0, 0, 0);
-            }
+                    for (int i = 0; i < 4; ++i) bv[i] = make_uint4(0, 0, 0, 0);
+                }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(b_s + sw128(brow, bp[i])) = bv[i];
-            // generic-proxy stores -> visible to the tensor core (async proxy)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&full_bar[s]);
-            cur = nxt;
+                for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(b_s + sw128(brow, bp[i])) = bv[i];
+                // generic-proxy stores -> visible to the tensor core (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&full_bar[s]);
+                cur = nxt;
+            }
         }
     } else if (warp == kTcTmaWarp) {
         if (lane == 0) {
@@ -396,8 +403,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
                     failed_s = 1;
                     break;
                 }
-                mbar_expect_tx(&aload_bar[s], (uint32_t)kTcATile);
+                mbar_expect_tx(&aload_bar[s], (uint32_t)(PRE ? kTcATile + kTcBTile : kTcATile));
                 tma_load_2d(ring + (size_t)s * kTcStage, &xmap, kb * kTcBK, (int)m0, &aload_bar[s]);
+                if (PRE) tma_load_2d(ring + (size_t)s * kTcStage + kTcATile, &wmap, kb * kTcBK, (int)n0, &aload_bar[s]);
                 issued = kb + 1;
             }
             // no copy may still be landing when the CTA exits
@@ -409,7 +417,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
         for (int kb = 0; kb < nkb; ++kb) {
             const int s = kb % kTcStages;
             if (!mbar_wait_bounded(&aload_bar[s], (uint32_t)((kb / kTcStages) & 1)) ||
-                !mbar_wait_bounded(&full_bar[s], (uint32_t)((kb / kTcStages) & 1)) || failed_s) {
+                (!PRE && !mbar_wait_bounded(&full_bar[s], (uint32_t)((kb / kTcStages) & 1))) || failed_s) {
                 atomicExch(p.err, kErrGemmWait);
                 failed_s = 1;
                 break;
@@ -458,6 +466,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const TcParams 
     }
 }
 
+// W dequantised once to f16 rows [n_pad][ld] (ld = k_pad) with the same
+// arithmetic and rounding as the producer warps (load_slice, dequant_half):
+// thread i takes half i % 2 of 64-column slice (i / 2) % nkb of row i / (2 nkb).
+template <int FMT>
+__global__ void tc_dequant_kernel(const TcParams p, __half* __restrict__ out, int64_t ld) {
+    const int nkb = (int)(ld / kTcBK);
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= p.n_pad * nkb * 2) return;
+    const int h = (int)(i & 1);
+    const int kb = (int)((i >> 1) % nkb);
+    const int64_t row = (i >> 1) / nkb;
+    RawSlice raw;
+    load_slice<FMT>(p, row, kb, h, raw);
+    uint4 v[4];
+    int pos[4];
+    dequant_half<FMT>(raw, kb, h, p.rtz != 0, v, pos);
+    uint4* dst = reinterpret_cast<uint4*>(out + row * ld + (int64_t)kb * kTcBK);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dst[pos[u]] = v[u];
+}
+
 // f32 rows -> contiguous f16 rows (the GEMM's activation operand).
 __global__ void to_f16_kernel(const float* __restrict__ x, int64_t ld, int64_t rows, int64_t k, __half* __restrict__ out) {
     const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -501,12 +530,39 @@ CUtensorMap activation_map(const __half* x, int64_t rows, int64_t k, int64_t ld)
     return map;
 }
 
+// [n_pad, k_pad] f16 weight rows, boxes of 64 columns x 256 rows, 128-byte swizzle.
+CUtensorMap weight_map(const __half* w, int64_t n_pad, int64_t k_pad) {
+    if (reinterpret_cast<uintptr_t>(w) & 15) invalid("tensor-core GEMM: the f16 weight scratch must be 16-byte aligned");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)k_pad, (cuuint64_t)n_pad};
+    const cuuint64_t strides[1] = {(cuuint64_t)k_pad * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBN};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(w), dims,
+                                            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(BEACON_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the GEMM weights");
+    return map;
+}
+
 template <int FMT>
-void launch_tc_t(const TcParams& p, const CUtensorMap& map, cudaStream_t s) {
-    auto kern = qgemm_tc_kernel<FMT>;
-    allow_max_dynamic_smem(kern);
+void launch_tc_t(const TcParams& p, const CUtensorMap& map, void* w16, int64_t k_pad, cudaStream_t s) {
     dim3 grid((unsigned)((p.m + kTcBM - 1) / kTcBM), (unsigned)((p.n + kTcBN - 1) / kTcBN));
-    kern<<<grid, kTcThreads, kTcSmem, s>>>(p, map);
+    if (w16) {
+        __half* wh = static_cast<__half*>(w16);
+        const int64_t threads = p.n_pad * (k_pad / kTcBK) * 2;
+        tc_dequant_kernel<FMT><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p, wh, k_pad);
+        BC_LAUNCHED("tc_dequant_kernel");
+        const CUtensorMap wmap = weight_map(wh, p.n_pad, k_pad);
+        auto kern = qgemm_tc_kernel<FMT, true>;
+        allow_max_dynamic_smem(kern);
+        kern<<<grid, kTcThreads, kTcSmem, s>>>(p, map, wmap);
+        BC_LAUNCHED("qgemm_tc_kernel");
+        return;
+    }
+    auto kern = qgemm_tc_kernel<FMT, false>;
+    allow_max_dynamic_smem(kern);
+    kern<<<grid, kTcThreads, kTcSmem, s>>>(p, map, map);
     BC_LAUNCHED("qgemm_tc_kernel");
 }
 
@@ -518,9 +574,11 @@ bool qgemm_tc_supported(const QLayout& L) {
 
 size_t qgemm_tc_scratch_bytes(int64_t rows, int64_t k) { return (size_t)(rows * k * 2 + 256); }
 
+size_t qgemm_tc_weight_scratch_bytes(const QLayout& L) { return (size_t)(L.n_pad * L.k_pad * 2); }
+
 void launch_qgemm_tc(const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld, int64_t rows, float* y,
                      int64_t y_ld, int epi, const float* res, int64_t res_ld, bool rtz, int* err, cudaStream_t s,
-                     void* x16_scratch, const QkvEpi* qkv) {
+                     void* x16_scratch, const QkvEpi* qkv, void* w16_scratch) {
     if (rows <= 0) return;
     if (!qgemm_tc_supported(L)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "tensor-core GEMM: unsupported block type");
     if (epi == EPI_QKV && !qkv) invalid("fused q/k/v epilogue launched without its destinations");
@@ -559,9 +617,9 @@ void launch_qgemm_tc(const QLayout& L, const void* w, const void* x, bool x_f16,
     if (qkv) p.qkv = *qkv;
     p.err = err;
     switch (L.dtype) {
-        case BEACON_CUDA_DTYPE_Q4_0: return launch_tc_t<FMT_Q4_0>(p, map, s);
-        case BEACON_CUDA_DTYPE_Q8_0: return launch_tc_t<FMT_Q8_0>(p, map, s);
-        default: return launch_tc_t<FMT_Q4_K>(p, map, s);
+        case BEACON_CUDA_DTYPE_Q4_0: return launch_tc_t<FMT_Q4_0>(p, map, w16_scratch, L.k_pad, s);
+        case BEACON_CUDA_DTYPE_Q8_0: return launch_tc_t<FMT_Q8_0>(p, map, w16_scratch, L.k_pad, s);
+        default: return launch_tc_t<FMT_Q4_K>(p, map, w16_scratch, L.k_pad, s);
     }
 }
 

@@ -295,3 +295,19 @@ def test_fast_prefill_tensor_core_attention_in_two_chunks(be, head_dim, heads, k
         ref = om.forward(prompt[lo:hi], lo)
         got = m.forward(prompt[lo:hi], lo)
         assert np.abs(got - ref).max() <= LOGITS_TOL, (lo, np.abs(got - ref).max())
+
+
+@pytest.mark.parametrize("dtype", ["Q8_0", "Q4_K", "Q4_0"])
+def test_fast_prefill_dequantise_first_gemm(be, dtype):
+    """A prefill chunk of 1100 rows takes the dequantise-first tensor-core
+    GEMM (weights dequantised once to f16 rows, both operands loaded by TMA)
+    for every layer linear; logits of all rows within the bar of the oracle."""
+    from beacon_cuda import _lib as L
+    c = small_cfg(num_layers=2, max_context=1152)
+    w = make_weights(oracle_cfg(c), getattr(orc, dtype), seed=95)
+    om = build_oracle_model(oracle_cfg(c), w)
+    m = cuda_model(be, c, w, numerics=L.NUMERICS_FAST, kv_dtype=L.DTYPE_F16)
+    prompt = list(np.random.default_rng(96).integers(0, c["vocab_size"], 1100))
+    ref = om.forward(prompt, 0)
+    got = m.forward(prompt, 0)
+    assert np.abs(got - ref).max() <= LOGITS_TOL, np.abs(got - ref).max()
