@@ -41,22 +41,29 @@ constexpr int kDecodeGemvRows = 64;  // decode steps up to this many sequences k
 // --- small kernels ------------------------------------------------------------
 
 // h[row] = E[tok[row]] (f32). Out-of-range ids write zeros and raise *err.
-// qy (hid % 32 == 0): also the first layer's quantised q/k/v input.
-__global__ void embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hid, const int32_t* tok, float* h,
-                             int* err, QxImage qy) {
+// qy (hid % 32 == 0): also the first layer's quantised q/k/v input. Grid
+// (rows, ceil(hid / 256)) of 256 threads, one element each: a row's loads
+// are all in flight at once (one CTA looping over the row waited for each
+// 256-element step in turn).
+constexpr int kEmbedThreads = 256;
+__global__ void __launch_bounds__(kEmbedThreads) embed_kernel(const void* E, int e_f16, int64_t vocab, int64_t hid,
+                                                              const int32_t* tok, float* h, int* err, QxImage qy) {
     pdl_trigger();
     pdl_wait();
     const int row = blockIdx.x;
     const int32_t t = tok[row];
     const bool ok = t >= 0 && t < vocab;
-    if (!ok && threadIdx.x == 0) atomicExch(err, kErrTokenRange);
-    for (int64_t i = threadIdx.x; i < hid; i += blockDim.x) {  // warp-uniform when hid % 32 == 0
-        float v = 0.0f;
-        if (ok) v = e_f16 ? __half2float(static_cast<const __half*>(E)[(int64_t)t * hid + i])
-                          : static_cast<const float*>(E)[(int64_t)t * hid + i];
-        h[(int64_t)row * hid + i] = v;
-        if (qy.data) qx_write_group(qy, row, i >> 5, (int)(i & 31), v, true);
-    }
+    if (!ok && threadIdx.x == 0 && blockIdx.y == 0) atomicExch(err, kErrTokenRange);
+    const int64_t i = (int64_t)blockIdx.y * kEmbedThreads + threadIdx.x;
+    if (i >= hid) return;  // whole warps when hid % 32 == 0
+    float v = 0.0f;
+    if (ok) v = e_f16 ? __half2float(static_cast<const __half*>(E)[(int64_t)t * hid + i])
+                      : static_cast<const float*>(E)[(int64_t)t * hid + i];
+    h[(int64_t)row * hid + i] = v;
+    if (qy.data) qx_write_group(qy, row, i >> 5, (int)(i & 31), v, true);
+}
+inline dim3 embed_grid(int rows, int64_t hid) {
+    return dim3((unsigned)rows, (unsigned)((hid + kEmbedThreads - 1) / kEmbedThreads));
 }
 
 // ops.rs:77-93 per row; w is f32. d % 4 == 0 and d <= 4 * 256 * kRmsVec: each
@@ -494,7 +501,8 @@ void decode_body(BeaconCudaModel* m, int batch, bool autoregressive, cudaStream_
     const QxImage qy = qx_active(m, batch, true)
                            ? qx_image(m, 0, m->Lqkv, batch, static_cast<const float*>(m->layers[0].attn_norm->ptr))
                            : QxImage{};
-    launch_kernel(embed_kernel, dim3(batch), dim3(256), 0, s, m->pdl, (const void*)m->embed->ptr,
+    launch_kernel(embed_kernel, embed_grid(batch, m->cfg.hidden_size), dim3(kEmbedThreads), 0, s, m->pdl,
+                  (const void*)m->embed->ptr,
                   (int)(m->embed_dtype == BEACON_CUDA_DTYPE_F16), (int64_t)m->cfg.vocab_size,
                   (int64_t)m->cfg.hidden_size, (const int32_t*)m->tok, m->h, m->err_dev, qy);
     run_layers(m, batch, true, m->pos_dev, 0, s);
@@ -951,8 +959,9 @@ int32_t beacon_cuda_model_forward(BeaconCudaModel* m, BeaconCudaStream* stream, 
             const int rows = std::min(m->max_rows, n_tokens - t0);
             for (int i = 0; i < rows; ++i) m->h_stage[i] = (int32_t)tokens[t0 + i];
             BC_CUDA(cudaMemcpyAsync(m->tok, m->h_stage, (size_t)rows * 4, cudaMemcpyHostToDevice, s));
-            embed_kernel<<<rows, 256, 0, s>>>(m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, V, c.hidden_size,
-                                              m->tok, m->h, m->err_dev, QxImage{});
+            embed_kernel<<<embed_grid(rows, c.hidden_size), kEmbedThreads, 0, s>>>(
+                m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, V, c.hidden_size, m->tok, m->h, m->err_dev,
+                QxImage{});
             BC_LAUNCHED("embed_kernel");
             run_layers(m, rows, false, nullptr, position + t0, s);
             finish_logits(m, rows, true, false, s);
