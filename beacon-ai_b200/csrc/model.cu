@@ -1175,11 +1175,36 @@ int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* m, BeaconCudaStream* s
                 default: return m->wlm->ptr;
             }
         };
-        // the kernels a decode step of `batch` sequences runs (or a prefill chunk's)
+        // the kernels a decode step of `batch` sequences runs (or a prefill chunk's),
+        // with the decode step's quantised-activation hand-offs where it uses
+        // them: o, gate/up and down read their input image (left valid by the
+        // decode steps run before) and write the next projection's
         m->gemm_rows = batch <= kDecodeGemvRows ? kDecodeGemvRows : 16;
+        const bool qxa = qx_active(m, batch, true) && m->layers[0].ffn_norm;
+        QxImage in{}, out{};
+        bool images = false;
+        const float* res = nullptr;  // o and down: the residual add of the decode step (into the scratch row)
+        if (qxa && slot == BEACON_CUDA_W_O) {
+            in = qx_image(m, 1, m->Lo, batch, nullptr);
+            out = qx_image(m, 0, m->Lgu, batch, static_cast<const float*>(m->layers[0].ffn_norm->ptr));
+            images = true;
+        } else if (qxa && slot == BEACON_CUDA_W_GATE) {
+            in = qx_image(m, 0, m->Lgu, batch, static_cast<const float*>(m->layers[0].ffn_norm->ptr));
+            out = qx_image(m, 2, m->Ld, batch, nullptr);
+            images = true;
+        } else if (qxa && slot == BEACON_CUDA_W_DOWN) {
+            in = qx_image(m, 2, m->Ld, batch, nullptr);
+            out = qx_image(m, 0, m->Lqkv, batch, static_cast<const float*>(m->layers[0].attn_norm->ptr));
+            images = true;
+        }
+        if (images && (slot == BEACON_CUDA_W_O || slot == BEACON_CUDA_W_DOWN)) {
+            epi = EPI_ADD;
+            res = m->h;
+        }
         auto pass = [&]() {
             for (int li = 0; li < nl; ++li)
-                linear(m, *Lp, weight(li), x, x_ld, batch, y, y_ld, epi, nullptr, 0, s);
+                linear(m, *Lp, weight(li), x, x_ld, batch, y, y_ld, epi, res, hid, s, nullptr,
+                       images ? &in : nullptr, images ? &out : nullptr);
         };
         pass();  // warm-up
         cudaEvent_t e0, e1;

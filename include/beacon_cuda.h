@@ -354,9 +354,13 @@ int32_t beacon_cuda_model_synchronize(BeaconCudaModel* model, BeaconCudaStream* 
  * L2-cold), with CUDA events on `stream`. slot: BEACON_CUDA_W_Q (the fused
  * q/k/v projection), _O, _GATE (the fused gate/up projection with SwiGLU),
  * _DOWN or _LM_HEAD. batch: rows, up to the model's row capacity; more than
- * 16 rows in the fast numerics run the prefill tensor-core GEMM. out_avg_us:
- * mean duration of one launch; out_bytes: algorithmic bytes of one launch
- * (weight blocks + f32 activations in + f32 out). */
+ * 16 rows in the fast numerics run the prefill tensor-core GEMM. Where the
+ * decode step hands quantised activations from kernel to kernel (fast
+ * numerics, f16 cache, one GPU), _O, _GATE and _DOWN run exactly as there:
+ * they read their input image (left by the decode steps run before) and
+ * write the next projection's, with the residual add for _O and _DOWN.
+ * out_avg_us: mean duration of one launch; out_bytes: algorithmic bytes of
+ * one launch (weight blocks + f32 activations in + f32 out). */
 int32_t beacon_cuda_model_profile_linear(BeaconCudaModel* model, BeaconCudaStream* stream, int32_t slot,
                                          int32_t batch, int32_t iters, float* out_avg_us,
                                          uint64_t* out_bytes);
