@@ -120,11 +120,12 @@ struct MmaTileRegs {
 
 template <int FMT>
 __device__ __forceinline__ void mma_load_tile(const uint8_t* tp, int lane, MmaTileRegs<FMT>& r) {
-    if (FMT == FMT_Q8_0) return;
+    if constexpr (FMT != FMT_Q8_0) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < 4; ++q)
 #pragma unroll
-        for (int mh = 0; mh < 2; ++mh) ldsm_chunk_pair(r.w[q][mh], tp, q, mh, lane);
+            for (int mh = 0; mh < 2; ++mh) ldsm_chunk_pair(r.w[q][mh], tp, q, mh, lane);
+    }
 }
 
 // A fragment of block j (0..7), half mh.
