@@ -354,7 +354,11 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
 // One pass of the decoder over `rows` rows that are either B sequences at
 // one position (decode) or consecutive tokens of sequence 0 (prefill chunk).
 // pos_ptr != nullptr: positions come from device memory (graph capture).
-void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, int pos_imm, cudaStream_t s) {
+// lm_rows: rows the final norm + lm_head run on -- all `rows` (-1), only the
+// last (1: a prefill chunk whose logits nobody reads, where time to first
+// token needs only the last row's argmax) or none (0: an earlier chunk).
+void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, int pos_imm, cudaStream_t s,
+                int lm_rows = -1) {
     m->gemm_rows = decode ? kDecodeGemvRows : 16;
     const auto& c = m->cfg;
     const int64_t hid = c.hidden_size;
@@ -475,14 +479,16 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
     }
     // final norm + lm_head (engine.rs:230-234)
+    if (lm_rows == 0) return;
+    const int lr = lm_rows < 0 ? rows : 1;
     {
         const float* fnw = static_cast<const float*>(m->final_norm->ptr);
-        const QxImage in = qxa ? qx_image(m, 0, m->Llm, rows, fnw) : QxImage{};
-        normed_linear(m, m->Llm, m->wlm->ptr, m->h, fnw, rows, m->logits_loc, m->v_loc, EPI_STORE, s, nullptr,
-                      qxa ? &in : nullptr);
+        const QxImage in = qxa && lm_rows < 0 ? qx_image(m, 0, m->Llm, rows, fnw) : QxImage{};
+        normed_linear(m, m->Llm, m->wlm->ptr, m->h + (int64_t)(rows - lr) * hid, fnw, lr, m->logits_loc, m->v_loc,
+                      EPI_STORE, s, nullptr, qxa && lm_rows < 0 ? &in : nullptr);
     }
     if (m->tp > 1) {
-        comm_all_gather(m->ctx, m->logits_loc, m->logits_all, (size_t)rows * m->v_loc, s);
+        comm_all_gather(m->ctx, m->logits_loc, m->logits_all, (size_t)lr * m->v_loc, s);
     }
 }
 
@@ -963,8 +969,10 @@ int32_t beacon_cuda_model_forward(BeaconCudaModel* m, BeaconCudaStream* stream, 
                 m->embed->ptr, m->embed_dtype == BEACON_CUDA_DTYPE_F16, V, c.hidden_size, m->tok, m->h, m->err_dev,
                 QxImage{});
             BC_LAUNCHED("embed_kernel");
-            run_layers(m, rows, false, nullptr, position + t0, s);
-            finish_logits(m, rows, true, false, s);
+            // without logits_out only the last row of the last chunk reaches the lm_head
+            const bool last_chunk = t0 + rows >= n_tokens;
+            run_layers(m, rows, false, nullptr, position + t0, s, logits_out ? -1 : (last_chunk ? 1 : 0));
+            if (logits_out || last_chunk) finish_logits(m, logits_out ? rows : 1, logits_out != nullptr, false, s);
             if (logits_out)
                 BC_CUDA(cudaMemcpyAsync(logits_out + (int64_t)t0 * V, full_logits(m), (size_t)rows * V * 4,
                                         cudaMemcpyDeviceToHost, s));

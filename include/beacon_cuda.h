@@ -315,7 +315,11 @@ int32_t beacon_cuda_model_set_weight(BeaconCudaModel* model, int32_t layer, int3
 /* Engine::reset_cache (engine.rs:176-180). */
 int32_t beacon_cuda_model_reset(BeaconCudaModel* model);
 /* Engine::forward (engine.rs:190-241) for one sequence: tokens (host) ->
- * logits [n_tokens, vocab] F32 written to host `logits_out` (NULL: skip). */
+ * logits [n_tokens, vocab] F32 written to host `logits_out`. NULL: no logits
+ * are returned, and only the last prompt row goes through the final norm and
+ * lm_head (its greedy token is computed; time to first token). Under tensor
+ * parallelism every rank passes logits_out, or NULL, alike: the two forms
+ * run different collectives. */
 int32_t beacon_cuda_model_forward(BeaconCudaModel* model, BeaconCudaStream* stream,
                                   const uint32_t* tokens, int32_t n_tokens, int32_t position,
                                   float* logits_out);
