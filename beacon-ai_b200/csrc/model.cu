@@ -194,6 +194,12 @@ struct BeaconCudaModel {
     std::unique_ptr<bc::DeviceBuffer> gemv_buf, attn_buf;
     std::unique_ptr<bc::DeviceBuffer> x16;  // f16 activations of the prefill GEMM
     std::unique_ptr<bc::DeviceBuffer> w16;  // f16 weights of one layer linear (dequantise-first GEMM)
+    // f16 copies of every layer linear, kept between prefills when they fit
+    // the budget (w16_keep: 0 undecided, 1 kept, -1 over budget); filled by
+    // the first prefill that uses each, dropped by any weight upload
+    std::map<const void*, std::unique_ptr<bc::DeviceBuffer>> w16_kept;
+    std::map<const void*, bool> w16_filled;
+    int w16_keep = 0;
     // decode hand-off of quantised activations between kernels (one GPU, fast
     // numerics, batch <= 8): the hidden-state image (q/k/v, gate/up, lm_head
     // inputs, with per-block sums of squares for their RMSNorm) and the
@@ -268,13 +274,40 @@ int gemv_rows(const BeaconCudaModel* m, const QLayout& L, int rem) {
 // would be repeated by every 256-row tile: 8 times at 2048 rows).
 constexpr int kDequantFirstRows = 1024;
 
-// The f16 weight scratch of the dequantise-first GEMM, sized for the largest
-// layer linear and allocated at its first use outside stream capture; NULL
-// while capturing (the fused form runs then).
-void* dequant_first_scratch(BeaconCudaModel* m, const QLayout& L, cudaStream_t s) {
+// The f16 weights of the dequantise-first GEMM for weight w. When the f16
+// copies of every layer linear fit 40% of the free device memory (decided at
+// the first use) each linear keeps its own copy, dequantised by its first
+// prefill only (*ready: already filled); otherwise one scratch sized for the
+// largest layer linear is refilled by every launch. Allocated outside stream
+// capture only: NULL while capturing (the fused form runs then).
+void* dequant_first_scratch(BeaconCudaModel* m, const QLayout& L, const void* w, cudaStream_t s, bool* ready) {
+    *ready = false;
     if (&L == &m->Llm) return nullptr;  // vocab-sized: not worth the memory
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     BC_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (m->w16_keep == 0 && cs == cudaStreamCaptureStatusNone) {
+        size_t total = 0;
+        for (const QLayout* l : {&m->Lqkv, &m->Lo, &m->Lgu, &m->Ld})
+            if (qgemm_tc_supported(*l)) total += qgemm_tc_weight_scratch_bytes(*l);
+        total *= m->layers.size();
+        size_t free_b = 0, total_b = 0;
+        BC_CUDA(cudaMemGetInfo(&free_b, &total_b));
+        m->w16_keep = total > 0 && total <= free_b / 10 * 4 ? 1 : -1;
+    }
+    if (m->w16_keep == 1) {
+        auto it = m->w16_kept.find(w);
+        if (it != m->w16_kept.end()) {
+            *ready = m->w16_filled[w];
+            m->w16_filled[w] = true;  // the launch this returns for fills it, in stream order
+            return it->second->ptr;
+        }
+        if (cs != cudaStreamCaptureStatusNone) return nullptr;
+        auto buf = std::make_unique<DeviceBuffer>(qgemm_tc_weight_scratch_bytes(L));
+        void* p = buf->ptr;
+        m->w16_kept[w] = std::move(buf);
+        m->w16_filled[w] = true;
+        return p;
+    }
     if (!m->w16) {
         if (cs != cudaStreamCaptureStatusNone) return nullptr;
         size_t bytes = 0;
@@ -297,8 +330,10 @@ void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x,
             qe = *qkv;
             qe.row0 = 0;
         }
+        bool ready = false;
+        void* w16 = rows >= kDequantFirstRows ? dequant_first_scratch(m, L, w, s, &ready) : nullptr;
         launch_qgemm_tc(L, w, x, false, x_ld, rows, y, y_ld, epi, res, res_ld, false, m->err_dev, s, m->x16->ptr,
-                        qkv ? &qe : nullptr, rows >= kDequantFirstRows ? dequant_first_scratch(m, L, s) : nullptr);
+                        qkv ? &qe : nullptr, w16, ready);
         return;
     }
     for (int r0 = 0, b = 0; r0 < rows; r0 += b) {
@@ -764,6 +799,10 @@ int32_t beacon_cuda_model_set_weight(BeaconCudaModel* m, int32_t layer, int32_t 
         require(m && data, "model_set_weight: null argument");
         set_device(m->ctx);
         release_graphs(m);
+        if (!m->w16_kept.empty()) BC_CUDA(cudaDeviceSynchronize());  // no queued prefill still reads them
+        m->w16_kept.clear();
+        m->w16_filled.clear();
+        m->w16_keep = 0;
         const auto& c = m->cfg;
         cudaStream_t s = m->ctx->internal;
         const bool dev = on_device != 0;

@@ -546,13 +546,15 @@ CUtensorMap weight_map(const __half* w, int64_t n_pad, int64_t k_pad) {
 }
 
 template <int FMT>
-void launch_tc_t(const TcParams& p, const CUtensorMap& map, void* w16, int64_t k_pad, cudaStream_t s) {
+void launch_tc_t(const TcParams& p, const CUtensorMap& map, void* w16, bool w16_ready, int64_t k_pad, cudaStream_t s) {
     dim3 grid((unsigned)((p.m + kTcBM - 1) / kTcBM), (unsigned)((p.n + kTcBN - 1) / kTcBN));
     if (w16) {
         __half* wh = static_cast<__half*>(w16);
-        const int64_t threads = p.n_pad * (k_pad / kTcBK) * 2;
-        tc_dequant_kernel<FMT><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p, wh, k_pad);
-        BC_LAUNCHED("tc_dequant_kernel");
+        if (!w16_ready) {
+            const int64_t threads = p.n_pad * (k_pad / kTcBK) * 2;
+            tc_dequant_kernel<FMT><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p, wh, k_pad);
+            BC_LAUNCHED("tc_dequant_kernel");
+        }
         const CUtensorMap wmap = weight_map(wh, p.n_pad, k_pad);
         auto kern = qgemm_tc_kernel<FMT, true>;
         allow_max_dynamic_smem(kern);
@@ -578,7 +580,7 @@ size_t qgemm_tc_weight_scratch_bytes(const QLayout& L) { return (size_t)(L.n_pad
 
 void launch_qgemm_tc(const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld, int64_t rows, float* y,
                      int64_t y_ld, int epi, const float* res, int64_t res_ld, bool rtz, int* err, cudaStream_t s,
-                     void* x16_scratch, const QkvEpi* qkv, void* w16_scratch) {
+                     void* x16_scratch, const QkvEpi* qkv, void* w16_scratch, bool w16_ready) {
     if (rows <= 0) return;
     if (!qgemm_tc_supported(L)) fail(BEACON_CUDA_ERR_UNSUPPORTED_DTYPE, "tensor-core GEMM: unsupported block type");
     if (epi == EPI_QKV && !qkv) invalid("fused q/k/v epilogue launched without its destinations");
@@ -617,9 +619,9 @@ void launch_qgemm_tc(const QLayout& L, const void* w, const void* x, bool x_f16,
     if (qkv) p.qkv = *qkv;
     p.err = err;
     switch (L.dtype) {
-        case BEACON_CUDA_DTYPE_Q4_0: return launch_tc_t<FMT_Q4_0>(p, map, w16_scratch, L.k_pad, s);
-        case BEACON_CUDA_DTYPE_Q8_0: return launch_tc_t<FMT_Q8_0>(p, map, w16_scratch, L.k_pad, s);
-        default: return launch_tc_t<FMT_Q4_K>(p, map, w16_scratch, L.k_pad, s);
+        case BEACON_CUDA_DTYPE_Q4_0: return launch_tc_t<FMT_Q4_0>(p, map, w16_scratch, w16_ready, L.k_pad, s);
+        case BEACON_CUDA_DTYPE_Q8_0: return launch_tc_t<FMT_Q8_0>(p, map, w16_scratch, w16_ready, L.k_pad, s);
+        default: return launch_tc_t<FMT_Q4_K>(p, map, w16_scratch, w16_ready, L.k_pad, s);
     }
 }
 

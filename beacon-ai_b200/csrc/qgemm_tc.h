@@ -22,9 +22,11 @@ size_t qgemm_tc_weight_scratch_bytes(const QLayout& L);
 // first dequantised into it as f16 rows (same values) and the GEMM loads both
 // operands by TMA instead of dequantising in its producer warps -- the form
 // for many rows, where the dequantisation would otherwise be repeated by
-// every row tile. *err = 4 if a bounded wait gave up.
+// every row tile. w16_ready: w16_scratch already holds this W's f16 rows (the
+// dequantisation is skipped). *err = 4 if a bounded wait gave up.
 void launch_qgemm_tc(const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld, int64_t rows, float* y,
                      int64_t y_ld, int epi, const float* res, int64_t res_ld, bool rtz, int* err, cudaStream_t s,
-                     void* x16_scratch, const QkvEpi* qkv = nullptr, void* w16_scratch = nullptr);
+                     void* x16_scratch, const QkvEpi* qkv = nullptr, void* w16_scratch = nullptr,
+                     bool w16_ready = false);
 
 }  // namespace bc

@@ -533,7 +533,8 @@ def run_prefill(a):
                       "model_shape": wl, "batch": NB, "prompt": P, "parallelism": "tp1"},
            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                         "frac": round(tflops / peak, 4), "traffic": None,
-                        "kernel": "qgemm_tc_kernel<Q8_0> (fused gate/up, M=%d N=%d K=%d), %.1f us/launch incl. the "
+                        "kernel": "qgemm_tc_kernel<Q8_0> (fused gate/up, M=%d N=%d K=%d; weights from the model's f16 "
+                                  "copies, dequantised by its first prefill and kept), %.1f us/launch incl. the "
                                   "f16 activation copy, peak %s (dense bf16)" % (P, 2 * F, H, gemm_us, peak_kind)}}
     model.close()
     del model

@@ -301,7 +301,9 @@ def test_fast_prefill_tensor_core_attention_in_two_chunks(be, head_dim, heads, k
 def test_fast_prefill_dequantise_first_gemm(be, dtype):
     """A prefill chunk of 1100 rows takes the dequantise-first tensor-core
     GEMM (weights dequantised once to f16 rows, both operands loaded by TMA)
-    for every layer linear; logits of all rows within the bar of the oracle."""
+    for every layer linear; logits of all rows within the bar of the oracle.
+    A second prefill after a cache reset reads the kept f16 copies (no
+    dequantisation pass) and gives the same logits."""
     from beacon_cuda import _lib as L
     c = small_cfg(num_layers=2, max_context=1152)
     w = make_weights(oracle_cfg(c), getattr(orc, dtype), seed=95)
@@ -311,3 +313,6 @@ def test_fast_prefill_dequantise_first_gemm(be, dtype):
     ref = om.forward(prompt, 0)
     got = m.forward(prompt, 0)
     assert np.abs(got - ref).max() <= LOGITS_TOL, np.abs(got - ref).max()
+    m.reset()
+    again = m.forward(prompt, 0)
+    assert np.array_equal(again, got)
