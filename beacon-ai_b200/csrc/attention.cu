@@ -451,9 +451,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const AttnR
 // accumulation. Key/value tiles of 64 keys are double-buffered in shared
 // memory by 16-byte asynchronous copies at swizzled positions (chunk ^ (row &
 // 7), conflict-free ldmatrix). Scores S = Q K^T with the pre-scaled query in
-// registers as f16 high and low parts (two MMAs, ~22-bit query precision);
-// online softmax on the accumulator fragments (row max and sum over the 4
-// lanes of a row); P rounded to f16 is re-packed in registers as the A
+// registers as f16 high and low parts (two MMAs, ~22-bit query precision),
+// pre-scaled by log2(e) so the softmax exponentials are exp2; online softmax
+// on the accumulator fragments (row max and sum over the 4 lanes of a row;
+// the causal / end-of-keys mask only on the tiles that cross a row's last
+// visible key); P rounded to f16 is re-packed in registers as the A
 // operand of O += P V, V^T fragments from transposing ldmatrix. The causal CTAs
 // are launched heaviest (latest query rows) first.
 constexpr int kPtKeys = 64;
@@ -492,6 +494,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(const At
     // as f16 high and low parts: regs (pair a, dims 2t..), (pair b, 2t..),
     // (pair a, 8 + 2t..), (pair b, 8 + 2t..)
     uint32_t qh[KS][4], ql[KS][4];
+    const float qscale = a.scale * 1.4426950408889634f;  // scores in log2 units: softmax by exp2
     {
         const float* q = reinterpret_cast<const float*>(a.q);
 #pragma unroll
@@ -505,8 +508,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(const At
                 float x0 = 0.0f, x1 = 0.0f;
                 if (row < a.sq) {
                     const float* qp = q + h * a.q_sh + row * a.q_ss + d;
-                    x0 = qp[0] * a.scale;
-                    x1 = qp[1] * a.scale;
+                    x0 = qp[0] * qscale;
+                    x1 = qp[1] * qscale;
                 }
                 const __half2 hh = __floats2half2_rn(x0, x1);
                 const float2 hf = __half22float2(hh);
@@ -517,8 +520,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(const At
     // keys [0, skv); causal: row s sees keys <= skv - sq + s
     const int64_t last_row = min((int64_t)a.sq - 1, r0 + RT - 1);
     const int64_t kend = a.causal ? min((int64_t)a.skv, a.skv - a.sq + last_row + 1) : (int64_t)a.skv;
-    const int64_t lim_a = a.causal ? (int64_t)a.skv - a.sq + row_a : (int64_t)a.skv - 1;
-    const int64_t lim_b = a.causal ? (int64_t)a.skv - a.sq + row_b : (int64_t)a.skv - 1;
+    // last visible key of each fragment row, also bounded by the keys there are
+    // (keys and rows fit 32 bits: the cache is at most 2^31 rows)
+    const int lim_a = (int)min(kend - 1, a.causal ? (int64_t)a.skv - a.sq + row_a : (int64_t)a.skv - 1);
+    const int lim_b = (int)min(kend - 1, a.causal ? (int64_t)a.skv - a.sq + row_b : (int64_t)a.skv - 1);
     const __half* kc = reinterpret_cast<const __half*>(a.k) + (int64_t)kvh * a.kv_sh;
     const __half* vc = reinterpret_cast<const __half*>(a.v) + (int64_t)kvh * a.kv_sh;
     const int ntiles = (int)((kend + kPtKeys - 1) / kPtKeys);
@@ -569,32 +574,41 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(const At
                 mma_f16(sc[n], ql[j + 1][0], ql[j + 1][1], ql[j + 1][2], ql[j + 1][3], b2, b3);
             }
         }
-        // mask and online softmax (rows a: sc[.][0..1], b: sc[.][2..3])
+        // mask (tiles crossing a row's last visible key) and online softmax
+        // (rows a: sc[.][0..1], b: sc[.][2..3])
+        const int kt0 = (int)k0;
+        if (kt0 + kPtKeys - 1 > min(lim_a, lim_b)) {
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int key = kt0 + 8 * n + 2 * t + e;
+                    if (key > lim_a) sc[n][e] = -INFINITY;
+                    if (key > lim_b) sc[n][2 + e] = -INFINITY;
+                }
+        }
         float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int64_t key = k0 + 8 * n + 2 * t + e;
-                if (key > lim_a || key >= kend) sc[n][e] = -INFINITY;
-                if (key > lim_b || key >= kend) sc[n][2 + e] = -INFINITY;
-                mx_a = fmaxf(mx_a, sc[n][e]);
-                mx_b = fmaxf(mx_b, sc[n][2 + e]);
-            }
+        for (int n = 0; n < NT; ++n) {
+            mx_a = fmaxf(mx_a, fmaxf(sc[n][0], sc[n][1]));
+            mx_b = fmaxf(mx_b, fmaxf(sc[n][2], sc[n][3]));
+        }
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
         const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-        const float c_a = m_a == -INFINITY ? 0.0f : expf(m_a - mn_a);
-        const float c_b = m_b == -INFINITY ? 0.0f : expf(m_b - mn_b);
+        const float c_a = m_a == -INFINITY ? 0.0f : exp2f(m_a - mn_a);
+        const float c_b = m_b == -INFINITY ? 0.0f : exp2f(m_b - mn_b);
+        // a row with no visible key yet keeps max -inf: its exponentials are 0
+        const float sa = mn_a == -INFINITY ? 0.0f : mn_a, sb = mn_b == -INFINITY ? 0.0f : mn_b;
         float su_a = 0.0f, su_b = 0.0f;
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                sc[n][e] = sc[n][e] == -INFINITY ? 0.0f : expf(sc[n][e] - mn_a);
-                sc[n][2 + e] = sc[n][2 + e] == -INFINITY ? 0.0f : expf(sc[n][2 + e] - mn_b);
+                sc[n][e] = exp2f(sc[n][e] - sa);  // exp2(-inf) = 0 for masked keys
+                sc[n][2 + e] = exp2f(sc[n][2 + e] - sb);
                 su_a += sc[n][e];
                 su_b += sc[n][2 + e];
             }
