@@ -69,8 +69,10 @@ inline dim3 embed_grid(int rows, int64_t hid) {
 // ops.rs:77-93 per row; w is f32. d % 4 == 0 and d <= 4 * 256 * kRmsVec: each
 // thread keeps its float4s in registers, so the row is read once.
 constexpr int kRmsVec = 8;
+// out16 (or NULL): also the f16 copy a tensor-core GEMM reads as its operand.
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                           float* __restrict__ out, int64_t d, float eps) {
+                                                           float* __restrict__ out, int64_t d, float eps,
+                                                           __half* __restrict__ out16) {
     __shared__ float sh[8];
     pdl_trigger();
     pdl_wait();
@@ -102,7 +104,13 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
         const int j = threadIdx.x + i * 256;
         if (j < n4) {
             const float4 g = wr[j];
-            o[j] = make_float4(v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w);
+            const float4 r = make_float4(v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w);
+            o[j] = r;
+            if (out16) {
+                const __half2 lo = __floats2half2_rn(r.x, r.y), hi = __floats2half2_rn(r.z, r.w);
+                reinterpret_cast<uint2*>(out16 + row * d)[j] =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+            }
         }
     }
 }
@@ -321,21 +329,29 @@ void* dequant_first_scratch(BeaconCudaModel* m, const QLayout& L, const void* w,
 
 // qkv (EPI_QKV only): destinations; chunk r0 is model row r0 onwards.
 // More than 16 rows in the fast numerics run as one tensor-core GEMM.
+bool takes_gemm(const BeaconCudaModel* m, const QLayout& L, int rows) {
+    return rows > m->gemm_rows && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L);
+}
+
+// The tensor-core GEMM of a linear; x is f32, or f16 when x_f16.
+void gemm_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const void* x, bool x_f16, int64_t x_ld,
+                 int rows, float* y, int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s,
+                 const QkvEpi* qkv) {
+    QkvEpi qe;
+    if (qkv) {
+        qe = *qkv;
+        qe.row0 = 0;
+    }
+    bool ready = false;
+    void* w16 = rows >= kDequantFirstRows ? dequant_first_scratch(m, L, w, s, &ready) : nullptr;
+    launch_qgemm_tc(L, w, x, x_f16, x_ld, rows, y, y_ld, epi, res, res_ld, false, m->err_dev, s, m->x16->ptr,
+                    qkv ? &qe : nullptr, w16, ready);
+}
+
 void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x, int64_t x_ld, int rows, float* y,
             int64_t y_ld, int epi, const float* res, int64_t res_ld, cudaStream_t s, const QkvEpi* qkv = nullptr,
             const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
-    if (rows > m->gemm_rows && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L)) {
-        QkvEpi qe;
-        if (qkv) {
-            qe = *qkv;
-            qe.row0 = 0;
-        }
-        bool ready = false;
-        void* w16 = rows >= kDequantFirstRows ? dequant_first_scratch(m, L, w, s, &ready) : nullptr;
-        launch_qgemm_tc(L, w, x, false, x_ld, rows, y, y_ld, epi, res, res_ld, false, m->err_dev, s, m->x16->ptr,
-                        qkv ? &qe : nullptr, w16, ready);
-        return;
-    }
+    if (takes_gemm(m, L, rows)) return gemm_linear(m, L, w, x, false, x_ld, rows, y, y_ld, epi, res, res_ld, s, qkv);
     for (int r0 = 0, b = 0; r0 < rows; r0 += b) {
         b = gemv_rows(m, L, rows - r0);
         LinearPlan pl = plan_linear(m->ctx, L, b, gemv_mode(m));
@@ -350,9 +366,10 @@ void linear(BeaconCudaModel* m, const QLayout& L, const void* w, const float* x,
     }
 }
 
-void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int rows, cudaStream_t s) {
+void rmsnorm(BeaconCudaModel* m, const float* x, const float* w, float* out, int rows, cudaStream_t s,
+             __half* out16 = nullptr) {
     launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, s, m->pdl, x, w, out, (int64_t)m->cfg.hidden_size,
-                  m->cfg.rms_norm_eps);
+                  m->cfg.rms_norm_eps, out16);
 }
 
 // y = W rmsnorm(x, norm_w): the norm rides in the persistent GEMV's staging
@@ -361,8 +378,15 @@ void normed_linear(BeaconCudaModel* m, const QLayout& L, const void* w, const fl
                    float* y, int64_t y_ld, int epi, cudaStream_t s, const QkvEpi* qkv = nullptr,
                    const QxImage* qx = nullptr, const QxImage* qy = nullptr) {
     const int64_t hid = m->cfg.hidden_size;
-    // the tensor-core GEMM takes the rows (linear() below): normalise first
-    bool fused = !(rows > m->gemm_rows && gemv_mode(m) == MODE_FAST && qgemm_tc_supported(L));
+    // the tensor-core GEMM takes the rows: normalise first, the norm writing
+    // the GEMM's f16 operand as well (no separate conversion)
+    if (takes_gemm(m, L, rows) && hid % 8 == 0) {
+        __half* x16 = static_cast<__half*>(m->x16->ptr);
+        rmsnorm(m, x, norm_w, m->xn, rows, s, x16);
+        gemm_linear(m, L, w, x16, true, hid, rows, y, y_ld, epi, nullptr, 0, s, qkv);
+        return;
+    }
+    bool fused = !takes_gemm(m, L, rows);
     for (int r0 = 0, b = 0; r0 < rows && fused; r0 += b) {
         b = gemv_rows(m, L, rows - r0);
         fused = plan_linear(m->ctx, L, b, gemv_mode(m)).v3;
