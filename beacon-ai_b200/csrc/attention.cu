@@ -648,17 +648,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(const At
 #pragma unroll
     for (int n = 0; n < ND; ++n) {
         const int d = 8 * n + 2 * t;
-        if (row_a < a.sq)
-            *reinterpret_cast<float2*>(a.out + ha * a.o_sh + row_a * a.o_ss + d) =
-                make_float2(o[n][0] * inv_a, o[n][1] * inv_a);
-        if (row_b < a.sq)
-            *reinterpret_cast<float2*>(a.out + hb * a.o_sh + row_b * a.o_ss + d) =
-                make_float2(o[n][2] * inv_b, o[n][3] * inv_b);
+        __half* o16 = static_cast<__half*>(a.out16);
+        if (row_a < a.sq) {
+            const float2 r = make_float2(o[n][0] * inv_a, o[n][1] * inv_a);
+            *reinterpret_cast<float2*>(a.out + ha * a.o_sh + row_a * a.o_ss + d) = r;
+            if (o16) *reinterpret_cast<__half2*>(o16 + ha * a.o_sh + row_a * a.o_ss + d) = __floats2half2_rn(r.x, r.y);
+        }
+        if (row_b < a.sq) {
+            const float2 r = make_float2(o[n][2] * inv_b, o[n][3] * inv_b);
+            *reinterpret_cast<float2*>(a.out + hb * a.o_sh + row_b * a.o_ss + d) = r;
+            if (o16) *reinterpret_cast<__half2*>(o16 + hb * a.o_sh + row_b * a.o_ss + d) = __floats2half2_rn(r.x, r.y);
+        }
     }
 }
 
 template <int D, int G>
-void launch_prefill_t(const AttnRowsArgs& a, cudaStream_t s) {
+bool launch_prefill_t(const AttnRowsArgs& a, cudaStream_t s) {
     constexpr int RT = kPfPairs / G;
     dim3 grid((unsigned)((a.sq + RT - 1) / RT), (unsigned)a.kv_heads);
     if (a.kv_f16 && a.kv_ss % 8 == 0 && a.kv_sh % 8 == 0 && a.q_ss % 2 == 0 && a.q_sh % 2 == 0 &&
@@ -667,7 +672,7 @@ void launch_prefill_t(const AttnRowsArgs& a, cudaStream_t s) {
                                      (int)PtLayout<D>::smem));
         prefill_attn_tc_kernel<D, G><<<grid, kPfThreads, PtLayout<D>::smem, s>>>(a);
         BC_LAUNCHED("prefill_attn_tc_kernel");
-        return;
+        return a.out16 != nullptr;
     }
     if (a.kv_f16) {
         allow_max_dynamic_smem(prefill_attn_kernel<D, G, __half>);
@@ -677,6 +682,7 @@ void launch_prefill_t(const AttnRowsArgs& a, cudaStream_t s) {
         prefill_attn_kernel<D, G, float><<<grid, kPfThreads, PfLayout<D>::bytes, s>>>(a);
     }
     BC_LAUNCHED("prefill_attn_kernel");
+    return false;
 }
 
 template <int D, int G>
@@ -760,8 +766,8 @@ bool prefill_attention_supported(const AttnRowsArgs& a) {
            a.o_ss % 4 == 0 && a.o_sh % 4 == 0;
 }
 
-void launch_prefill_attention(const AttnRowsArgs& a, cudaStream_t s) {
-    if (a.sq == 0 || a.skv == 0) return;
+bool launch_prefill_attention(const AttnRowsArgs& a, cudaStream_t s) {
+    if (a.sq == 0 || a.skv == 0) return false;
     if (!prefill_attention_supported(a)) invalid("prefill attention: unsupported layout");
     const int G = (int)(a.heads / a.kv_heads);
     if (a.d == 128) {

@@ -27,12 +27,14 @@ struct AttnRowsArgs {
     int64_t q_sb, q_sh, q_ss;
     int64_t kv_sb, kv_sh, kv_ss;
     int64_t o_sb, o_sh, o_ss;
+    void* out16 = nullptr;  // tensor-core prefill kernel: also an f16 copy of out (same layout)
 };
 void launch_attention_rows(const AttnRowsArgs& a, cudaStream_t s);
 // Tiled prefill attention (one sequence, no additive mask, f32 q): 128
 // (row, head) pairs of one KV head per CTA share each staged key/value tile.
 bool prefill_attention_supported(const AttnRowsArgs& a);
-void launch_prefill_attention(const AttnRowsArgs& a, cudaStream_t s);
+// True when the f16 copy (a.out16) was written too (the tensor-core kernel ran).
+bool launch_prefill_attention(const AttnRowsArgs& a, cudaStream_t s);
 
 // Split-K decode attention over KV caches laid out [batch][max_ctx][kv_heads][d].
 // q: f32 [batch][heads][d]; out: f32 [batch][heads][d]. Scratch: part_acc

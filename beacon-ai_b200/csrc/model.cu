@@ -453,6 +453,7 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
                           qxa ? &in : nullptr);
         }
         const float scale = 1.0f / sqrtf((float)D);  // engine.rs:415
+        bool o16 = false;  // the attention also wrote the o GEMM's f16 operand
         if (decode) {
             DecodeAttnArgs a{};
             a.q = m->q;
@@ -503,10 +504,13 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
             a.o_sb = 0;
             a.o_sh = D;
             a.o_ss = m->qd;
+            // the o projection's tensor-core GEMM reads an f16 copy the
+            // attention writes beside its f32 output
+            if (takes_gemm(m, m->Lo, rows) && m->qd % 8 == 0) a.out16 = m->x16->ptr;
             // the tiled kernel in the fast numerics; the row kernel keeps the
             // reference's summation order for the exact ones
             if (gemv_mode(m) == MODE_FAST && prefill_attention_supported(a))
-                launch_prefill_attention(a, s);
+                o16 = launch_prefill_attention(a, s);
             else
                 launch_attention_rows(a, s);
         }
@@ -515,8 +519,12 @@ void run_layers(BeaconCudaModel* m, int rows, bool decode, const int* pos_ptr, i
         {
             const QxImage in = qxa ? qx_image(m, 1, m->Lo, rows, nullptr) : QxImage{};
             const QxImage out = qxa ? qx_image(m, 0, m->Lgu, rows, ffn_nw) : QxImage{};
-            linear(m, m->Lo, L.wo->ptr, m->attn, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE,
-                   r0 ? m->h : nullptr, hid, s, nullptr, qxa ? &in : nullptr, qxa ? &out : nullptr);
+            if (o16)
+                gemm_linear(m, m->Lo, L.wo->ptr, m->x16->ptr, true, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE,
+                            r0 ? m->h : nullptr, hid, s, nullptr);
+            else
+                linear(m, m->Lo, L.wo->ptr, m->attn, m->qd, rows, m->h, hid, r0 ? EPI_ADD : EPI_STORE,
+                       r0 ? m->h : nullptr, hid, s, nullptr, qxa ? &in : nullptr, qxa ? &out : nullptr);
         }
         comm_all_reduce_sum(m->ctx, m->h, (size_t)rows * hid, s);
         {
